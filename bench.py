@@ -1,0 +1,374 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path (one JSON line on rank 0).
+
+Headline: FlashAttention forward, fp16, causal,
+q/k/v [B=4, H=16, S=2048, D=128] ~ N(0,1)*0.5, TFLOP/s with causal FLOPs =
+2*B*H*S^2*D. The same run also measures the GEMM (8192^3 fp16 + bias + ReLU,
+TFLOP/s) and the row family (X[65536, 4096] fp32, GB/s), reported under
+"extra".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2|reference]
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same per-rank
+workload on its own shard of (batch, head) units ("weak" scaling, no data-path
+collective); value = all ranks' FLOPs / max-over-ranks device time.
+Timing: CUDA events around each launch on the launching stream; L2 (126 MB) is
+flushed by writing a 256 MB buffer between timed launches, outside the events.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes from the committed ncu summary (kernel -> bytes)."""
+    p = ROOT / "profiles" / "traffic.txt"
+    out = {}
+    if p.exists():
+        for line in p.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                r = subprocess.run(["nvidia-smi", "-i", str(self.gpu),
+                                    f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                                   capture_output=True, text=True, timeout=5)
+                if r.returncode == 0 and r.stdout.strip():
+                    self.samples.append([s.strip() for s in r.stdout.strip().split(",")])
+            except Exception:
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 5 + i and s[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend)
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_launches(fn, steps, warmup, flush_buf, world):
+    """Device time per launch (ms): events around each launch, L2 flushed between."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = []
+    st = torch.cuda.current_stream()
+    for _ in range(steps):
+        flush_buf.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    barrier(world)
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def cpu_sample_fa(cfg, seconds=8.0):
+    """Time the oracle (fp32 torch-CPU restatement of the reference's FA oracle)
+    on single (batch, head) slices of cfg; returns (TFLOP/s, threads, sample)."""
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    one = W.FAConfig("sample", 1, 1, cfg.S, cfg.D, cfg.causal, cfg.dtype, cfg.std)
+    q, k, v = W.fa_inputs(one, seed=1)
+    O.ref_attention(q, k, v, cfg.causal)  # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 2:
+        O.ref_attention(q, k, v, cfg.causal)
+        n += 1
+    dt = time.perf_counter() - t0
+    tflops = one.flops() * n / dt / 1e12
+    return tflops, threads, f"{n} x one (b,h) head [1,1,{cfg.S},{cfg.D}] causal={cfg.causal} fp32 in {dt:.1f}s"
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's CPU oracle path for FA (the reference's
+    Metal kernels cannot run here), timed on this host's cores, same metric."""
+    if rank != 0:
+        return
+    from triton_msl_b200 import workloads as W
+    cfg = W.FA_F16_CAUSAL
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    heads = 2
+    samp = W.FAConfig("sample", 1, heads, cfg.S, cfg.D, cfg.causal, cfg.dtype, cfg.std)
+    q, k, v = W.fa_inputs(samp, seed=1)
+    for _ in range(args.warmup):
+        O.ref_attention(q, k, v, cfg.causal)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.ref_attention(q, k, v, cfg.causal)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    val = samp.flops() / (ms / 1e3) / 1e12
+    sample = f"{heads} (b,h) heads of [4,16,2048,128] causal per step, fp32 torch-CPU oracle"
+    print(json.dumps({
+        "impl": "reference", "metric": "fa_fwd_fp16_causal_d128_tflops", "value": round(val, 5),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
+                   "causal": True, "sample": sample},
+        "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def roofline(name, achieved, peak, unit, bound, traffic, per_launch_units, peak_kind):
+    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
+            "unit": unit, "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+            "traffic": traffic.get(name) if traffic else None}
+
+
+def run_b2(args, world, rank, local):
+    import triton_msl_b200 as b2
+    from triton_msl_b200 import workloads as W
+    dev = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_kind = load_peaks()
+    traffic = load_traffic()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    # ---------------- headline: FA fp16 causal D=128 ----------------
+    cfg = W.FA_F16_CAUSAL
+    q, k, v = W.fa_inputs(cfg, device=dev, seed=rank)
+    fa = lambda: b2.flash_attn_fwd(q, k, v, causal=True)
+    fa()
+    kern = b2.last_kernel()
+    if kern != "fa_sm100":
+        raise RuntimeError(f"headline FA ran on {kern}, not the tensor-core kernel")
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    try:
+        times = time_launches(fa, args.steps, args.warmup, flush, world)
+    finally:
+        if sampler:
+            sampler.__exit__()
+    ms_rank = statistics.mean(times)
+    ms = max_over_ranks(ms_rank, world)
+    flops = cfg.flops()
+    value = world * flops / (ms / 1e3) / 1e12
+    peak_tc = float(peaks["bf16_tflops"])
+    rl = roofline("fa_sm100", flops / (ms / 1e3) / 1e12, peak_tc, "TFLOP/s", "tensor", traffic,
+                  1, peak_kind)
+
+    # e2e through the public op with pinned host buffers, copies inside the timed region
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty_like(hq).pin_memory()
+    def e2e_step():
+        dq, dk, dv = (h.to(dev, non_blocking=True) for h in (hq, hk, hv))
+        o = b2.flash_attn_fwd(dq, dk, dv, causal=True)
+        ho.copy_(o, non_blocking=True)
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    st = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    bev = torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    bev.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(bev) / args.steps, world)
+    e2e_val = world * flops / (e2e_ms / 1e3) / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = ho.numel() * ho.element_size()
+    del hq, hk, hv, ho
+
+    extra = {}
+    launches = args.steps  # headline timed region: one fa_sm100 launch per step
+    if not args.headline_only:
+        extra = run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic)
+
+    if rank != 0:
+        return
+    clocks = sampler.summary() if sampler else None
+    cpu_val, cores, sample = cpu_sample_fa(cfg, seconds=args.cpu_seconds)
+    line = {
+        "metric": "fa_fwd_fp16_causal_d128_tflops", "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
+                   "causal": True, "flops_per_step_per_gpu": flops,
+                   "l2": "flushed between timed launches (256 MB write)",
+                   "parallelism": f"(batch,head) shards x{world}, no collective"},
+        "roofline": rl,
+        "cpu_baseline": {"value": round(cpu_val, 5), "unit": "TFLOP/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "extra": extra,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic):
+    """GEMM 8192^3 + bias + ReLU and the row family at 65536x4096, same timing rules."""
+    import triton_msl_b200 as b2
+    from triton_msl_b200 import workloads as W
+    out = {}
+    steps = max(3, min(args.steps, 10))
+    g = W.GEMM_F16
+    a, bm, bias = W.gemm_inputs(g, device=dev, seed=rank)
+    fn = lambda: b2.gemm(a, bm, bias, "relu", torch.float16)
+    fn()
+    kname = b2.last_kernel()
+    ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+    ach = g.flops() / (ms / 1e3) / 1e12
+    out[g.name] = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                   "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s",
+                                        "tensor", traffic, 1, peak_kind)}
+    del a, bm, bias
+    r = W.ROWS_F32
+    x, w, bb = W.row_inputs(r, device=dev, seed=rank)
+    ops = {"softmax": lambda: b2.row_softmax(x),
+           "layernorm": lambda: b2.row_layernorm(x, w, bb, 1e-5),
+           "rmsnorm": lambda: b2.row_rmsnorm(x, w, 1e-6),
+           "sum": lambda: b2.row_sum(x), "max": lambda: b2.row_max(x),
+           "argmax": lambda: b2.row_argmax(x)}
+    for op, fn in ops.items():
+        fn()
+        kname = b2.last_kernel()
+        ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+        gbs = r.bytes(op) / (ms / 1e3) / 1e9
+        out[f"{r.name}_{op}"] = {"value": round(world * gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
+                                 "roofline": roofline(f"{kname}_{op}", gbs, float(peaks["hbm_gbs"]),
+                                                      "GB/s", "hbm", traffic, 1, peak_kind)}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
+    ap.add_argument("--headline-only", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_b2(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

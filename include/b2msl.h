@@ -1,0 +1,158 @@
+/*
+ * b2msl.h — C ABI of the B200 (sm_100a) hot-path kernels that replace the
+ * Metal template path of triton-msl (FlashAttention forward, fast matmul with
+ * bias/activation epilogue, row-reduction family).
+ *
+ * Conventions (all entry points):
+ *  - Plain device pointers and sizes; strides are in ELEMENTS, like the stride
+ *    arguments the reference's Triton kernels receive.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *    stream-ordered and asynchronous; nothing synchronises the host.
+ *  - The library never allocates device memory on these paths; scratch space,
+ *    where a path needs it, is passed in (`workspace`, sized by
+ *    b2_query_workspace()).
+ *  - Return 0 on success or a negative B2_E* status. Validation happens before
+ *    any launch, so a failed call has launched nothing. The reference raises
+ *    MetalNonRecoverableError instead of producing wrong numbers
+ *    (triton_msl/errors.py:82-102); this ABI returns B2_EINVAL/B2_EUNSUPPORTED
+ *    and the message is available from b2_last_error() on the same thread.
+ *  - Device-side waits are bounded; a wedged pipeline sets a bit in the
+ *    device status word (b2_device_status) instead of hanging.
+ */
+#ifndef B2MSL_H_
+#define B2MSL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* status codes */
+#define B2_OK 0
+#define B2_EINVAL (-1)       /* bad shape / stride / pointer / dtype combination */
+#define B2_EUNSUPPORTED (-2) /* valid request this build does not implement */
+#define B2_ELAUNCH (-3)      /* CUDA runtime error while launching */
+#define B2_ETIMEOUT (-4)     /* a bounded device wait expired (see b2_device_status) */
+
+/* element types */
+#define B2_F32 0
+#define B2_F16 1
+#define B2_BF16 2
+#define B2_I64 3
+
+/* GEMM epilogue activations (reference op table: triton_msl/codegen/_lowerer_templates.py:1733-1748) */
+#define B2_ACT_NONE 0
+#define B2_ACT_RELU 1
+#define B2_ACT_GELU 2      /* exact erf GELU */
+#define B2_ACT_GELU_TANH 3 /* tanh-approximated GELU */
+#define B2_ACT_SILU 4
+
+/* row operations (b2_row_op) */
+#define B2_ROW_SOFTMAX 0
+#define B2_ROW_LAYERNORM 1
+#define B2_ROW_RMSNORM 2
+#define B2_ROW_SUM 3
+#define B2_ROW_MAX 4
+#define B2_ROW_ARGMAX 5
+#define B2_ROW_MIN 6
+#define B2_ROW_ARGMIN 7
+
+/* Library version, e.g. "b2msl 0.1.0 sm_100a". */
+const char* b2_version(void);
+
+/* Last error message of the calling thread ("" if none). */
+const char* b2_last_error(void);
+
+/* Kernel family the calling thread's last successful call launched
+ * ("fa_sm100", "fa_simt", "gemm_sm100", "gemm_simt", "row_reduce", "row_split",
+ * "row_memset"). Introspection for tests and benchmarks; the reference's
+ * equivalent is its TRITON_MSL_PATH_LOG lowering-path log
+ * (triton_msl/codegen/msl_emitter.py:523-538). */
+const char* b2_last_kernel(void);
+
+/*
+ * FlashAttention forward: o = softmax(sm_scale * q @ k^T [+ causal mask]) @ v.
+ *
+ * Replaces the reference FA entry: the @triton.jit kernel `_flash_attn_fwd`
+ * (tests/test_flash_attention.py:35-118) lowered to the simdgroup template
+ * `make_flash_attention_kernel_simdgroup` (triton_msl/codegen/_msl_templates.py:1833-2070),
+ * whose buffer ABI is (Q, K, V, Out, 16 strides in the order
+ * q.zhmk, k.zhnk, v.zhnk, o.zhmk, Z, H, N_CTX) (_msl_templates.py:2108-2121).
+ * Here Z=B, N_CTX=S; strides[16] is that same 16-stride list in elements.
+ * q, k, v and o share `dtype` (B2_F32, B2_F16 or B2_BF16); accumulation is
+ * fp32. The causal mask keeps key j for query i iff j <= i; rows with no
+ * unmasked key produce zeros (reference oracle nan_to_num, tests/test_flash_attention.py:124-135).
+ */
+int b2_fa_fwd(const void* q, const void* k, const void* v, void* o,
+              int64_t B, int64_t H, int64_t S, int64_t D,
+              const int64_t strides[16], float sm_scale, int causal, int dtype,
+              void* stream);
+
+/*
+ * GEMM with fused epilogue: C = act(alpha * (A @ B) + bias[None, :]).
+ *
+ * Replaces the fast-matmul template `make_simdgroup_matmul_kernel_fast`
+ * (triton_msl/codegen/_msl_templates.py:4134-4255) dispatched by
+ * `dispatch_fast_matmul` (triton_msl/autotuning/_fast_matmul_dispatch.py:27-158)
+ * and the staged epilogue template (_lowerer_templates.py:1515-1855). Stride
+ * arguments follow the reference's `mm` kernel (tests/test_fast_matmul_parity.py:14-27):
+ * strides[6] = {s_am, s_ak, s_bk, s_bn, s_cm, s_cn} in elements.
+ * in_dtype applies to A and B; bias (may be NULL) has bias_dtype; C has out_dtype.
+ * fp32 inputs are computed in fp32 FMA (no TF32 rounding).
+ * workspace/ws_bytes: scratch as reported by b2_query_workspace (may be NULL/0
+ * when that reports 0).
+ */
+int b2_gemm(const void* A, const void* Bm, const void* bias, void* C,
+            int64_t M, int64_t N, int64_t K, const int64_t strides[6],
+            float alpha, int act, int in_dtype, int bias_dtype, int out_dtype,
+            void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * Row operation over x[rows, cols] (row stride ld_x elements, unit column stride).
+ *
+ * Replaces the reference row family: the TG-cached softmax / LayerNorm
+ * templates (triton_msl/codegen/_lowerer_templates.py:992-1320), the generic
+ * tt.reduce lowering for sum/max/argmax (_lowerer_reduce.py:773-1333) and the
+ * prebuilt make_row_reduce_kernel / make_softmax_kernel / make_rms_norm_kernel /
+ * make_layer_norm_kernel ABIs (_msl_templates.py:259-449, 888-1090).
+ *   SOFTMAX:   out[r, :] = softmax(x[r, :])                       (out like x)
+ *   LAYERNORM: out = (x - mean) * rsqrt(var + eps) * w + b      (w, b may be NULL)
+ *   RMSNORM:   out = x * rsqrt(mean(x^2) + eps) * w               (w may be NULL)
+ *   SUM/MAX/MIN: out[r] = reduce(x[r, :])        (out has x's dtype, NaN propagates)
+ *   ARGMAX/ARGMIN: out[r] = int64 index; ties -> lowest index; a NaN counts as
+ *              the extreme value (first NaN wins), matching torch.argmax.
+ * w and b have x's dtype. ld_out is the output row stride (elements) for the
+ * row-shaped outputs and ignored for the per-row scalars.
+ * workspace: scratch for the split-row path used when rows are few and long;
+ * size from b2_query_workspace (0 for most shapes).
+ */
+int b2_row_op(int op, const void* x, const void* w, const void* b, void* out,
+              int64_t rows, int64_t cols, int64_t ld_x, int64_t ld_out,
+              float eps, int dtype, void* workspace, size_t ws_bytes,
+              void* stream);
+
+/* Scratch bytes a call with these arguments needs (0 = none).
+ * kind: 0 = b2_gemm (a0=M, a1=N, a2=K, a3=in_dtype),
+ *       1 = b2_row_op (a0=op, a1=rows, a2=cols, a3=dtype),
+ *       2 = b2_fa_fwd (always 0). */
+size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3);
+
+/* OR of the device status bits written by bounded waits on `device` since the
+ * last clear (0 = no wait expired). Synchronises that device. clear != 0 resets it. */
+int b2_device_status(int device, int clear, uint32_t* status_out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}  // extern "C"
+#endif
+
+#endif  /* B2MSL_H_ */

@@ -1,0 +1,277 @@
+"""GPU parity: every kernel family against the CPU oracle on the same seeded inputs.
+
+Tolerances (written per test): fp32 paths max-abs <= 1e-4; fp16/bf16 paths
+normwise-relative <= 2e-3 (max|got-ref| / max|ref|); argmax/argmin bit-exact.
+Cases mirror the reference's parity tests: FA over dtype x causal x unaligned N
+(tests/test_fa_simdgroup_diff.py:38-57), matmul shapes of
+tests/test_fast_matmul_parity.py:47-62, reduce forms of tests/test_fuzz_reduce.py.
+"""
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import triton_msl_b200 as b2
+from oracle import oracle as O
+from triton_msl_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+F32_ABS, LOWP_REL = O.TOL_F32_ABS, O.TOL_LOWP_REL
+
+
+def _rand(shape, dtype, seed, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std).to(dtype)
+
+
+def _check(got, ref, dtype):
+    if dtype == torch.float32:
+        err = O.max_abs_err(got, ref)
+        assert err <= F32_ABS, f"max-abs {err:.3e} > {F32_ABS}"
+    else:
+        err = O.normwise_err(got, ref)
+        assert err <= LOWP_REL, f"normwise {err:.3e} > {LOWP_REL}"
+
+
+# ------------------------------------------------------------------ attention
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("S", [50, 100, 128, 192, 256, 600])
+def test_fa_tensor_core_matches_oracle(dtype, D, causal, S):
+    q, k, v = (_rand((1, 2, S, D), dtype, s, 0.5) for s in (1, 2, 3))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    assert b2.last_kernel() == "fa_sm100"
+    _check(o, O.ref_attention(q, k, v, causal), dtype)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_fa_long_sequence_bf16_causal(D):
+    q, k, v = (_rand((2, 2, 2048, D), torch.bfloat16, s, 0.5) for s in (4, 5, 6))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+    assert b2.last_kernel() == "fa_sm100"
+    _check(o, O.ref_attention(q, k, v, True), torch.bfloat16)
+
+
+def test_fa_config1_fp32():
+    """fp32 non-causal [1,4,256,64], N(0,1) seed 0, scale 1/8."""
+    q, k, v = W.fa_inputs(W.FA_F32, seed=0)
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=False, sm_scale=1 / 8)
+    assert b2.last_kernel() == "fa_simt"
+    _check(o, O.ref_attention(q, k, v, False, 1 / 8), torch.float32)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("S,D", [(50, 32), (100, 64), (192, 128), (77, 48)])
+def test_fa_fp32_unaligned(causal, S, D):
+    q, k, v = (_rand((2, 3, S, D), torch.float32, s) for s in (7, 8, 9))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    _check(o, O.ref_attention(q, k, v, causal), torch.float32)
+
+
+def test_fa_strided_layouts():
+    """[B,S,H,D] storage viewed as [B,H,S,D] stays on tensor cores; a non-unit
+    inner stride goes to the CUDA-core kernel. Both must match."""
+    base = _rand((2, 300, 4, 128), torch.float16, 11, 0.5).to(DEV)
+    q = base.permute(0, 2, 1, 3)
+    k = _rand((2, 300, 4, 128), torch.float16, 12, 0.5).to(DEV).permute(0, 2, 1, 3)
+    v = _rand((2, 300, 4, 128), torch.float16, 13, 0.5).to(DEV).permute(0, 2, 1, 3)
+    o = b2.flash_attn_fwd(q, k, v, causal=True)
+    assert b2.last_kernel() == "fa_sm100"
+    ref = O.ref_attention(q.cpu(), k.cpu(), v.cpu(), True)
+    _check(o, ref, torch.float16)
+    qs = _rand((1, 2, 64, 128 * 2), torch.float16, 14, 0.5).to(DEV)[..., ::2]
+    ks = _rand((1, 2, 64, 128), torch.float16, 15, 0.5).to(DEV)
+    vs = _rand((1, 2, 64, 128), torch.float16, 16, 0.5).to(DEV)
+    o2 = b2.flash_attn_fwd(qs, ks, vs, causal=False)
+    assert b2.last_kernel() == "fa_simt"
+    _check(o2, O.ref_attention(qs.cpu(), ks.cpu(), vs.cpu(), False), torch.float16)
+
+
+def test_fa_custom_scale():
+    q, k, v = (_rand((1, 2, 256, 64), torch.float16, s, 0.5) for s in (21, 22, 23))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=True, sm_scale=0.3)
+    _check(o, O.ref_attention(q, k, v, True, 0.3), torch.float16)
+
+
+def test_fa_golden_fixtures():
+    gold = np.load(Path(__file__).parent / "golden" / "golden.npz")
+    meta = json.loads(bytes(gold["__meta__"]).decode())
+    for m in meta:
+        if not m["name"].startswith("fa_"):
+            continue
+        t = {k: torch.from_numpy(gold[f"{m['name']}/{k}"].copy()) for k in "qkvo"}
+        causal = bool(gold[f"{m['name']}/causal"])
+        o = b2.flash_attn_fwd(t["q"].to(DEV), t["k"].to(DEV), t["v"].to(DEV), causal=causal)
+        _check(o, t["o"], t["q"].dtype)
+
+
+# ----------------------------------------------------------------------- gemm
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 2048), (512, 512, 512), (256, 2080, 256),
+                                   (256, 256, 264), (1024, 512, 256), (300, 200, 136)])
+def test_gemm_tensor_core_matches_oracle(dtype, M, N, K):
+    a = _rand((M, K), dtype, 31, 1 / math.sqrt(K))
+    b = _rand((K, N), dtype, 32, 1 / math.sqrt(K))
+    c = b2.gemm(a.to(DEV), b.to(DEV))
+    assert b2.last_kernel() == "gemm_sm100"
+    _check(c, O.ref_gemm(a, b, out_dtype=torch.float32), dtype)
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "gelu", "gelu_tanh", "silu"])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32, torch.bfloat16])
+def test_gemm_epilogue(act, out_dtype):
+    M, N, K = 384, 640, 512
+    a = _rand((M, K), torch.float16, 41, 1 / math.sqrt(K))
+    b = _rand((K, N), torch.float16, 42, 1 / math.sqrt(K))
+    bias = _rand((N,), torch.float32, 43, 0.1)
+    c = b2.gemm(a.to(DEV), b.to(DEV), bias.to(DEV), act, out_dtype)
+    assert c.dtype == out_dtype
+    _check(c, O.ref_gemm(a, b, bias, act, torch.float32), torch.float16)
+
+
+def test_gemm_k_major_b_linear_layout():
+    """x @ w.t() (nn.Linear): B is K-major; still the tensor-core kernel."""
+    x = _rand((777, 1024), torch.bfloat16, 51, 1 / 32)
+    w = _rand((1536, 1024), torch.bfloat16, 52, 1 / 32)
+    bias = _rand((1536,), torch.bfloat16, 53, 0.1)
+    c = b2.gemm(x.to(DEV), w.to(DEV).t(), bias.to(DEV), "relu")
+    assert b2.last_kernel() == "gemm_sm100"
+    _check(c, O.ref_gemm(x, w.t(), bias, "relu", torch.float32), torch.bfloat16)
+
+
+def test_gemm_config3_prime_fp32():
+    """fp32 inputs at 2048^3 (BASELINE config 3'), max-abs 1e-4."""
+    cfg = W.GEMM_F32
+    a, b, _ = W.gemm_inputs(cfg, seed=0)
+    c = b2.gemm(a.to(DEV), b.to(DEV))
+    assert b2.last_kernel() == "gemm_simt"
+    _check(c, O.ref_gemm(a, b), torch.float32)
+
+
+def test_gemm_odd_strides_fall_back_to_cuda_cores():
+    a = _rand((130, 70), torch.float16, 61, 0.1)   # K=70: rows not 16-byte pitched
+    b = _rand((70, 90), torch.float16, 62, 0.1)
+    c = b2.gemm(a.to(DEV), b.to(DEV), activation="relu")
+    assert b2.last_kernel() == "gemm_simt"
+    _check(c, O.ref_gemm(a, b, None, "relu", torch.float32), torch.float16)
+
+
+def test_gemm_config3_full_size_sampled():
+    """BASELINE config 3 at full size (8192^3 + bias + ReLU, fp16 out), checked on
+    sampled row blocks against the fp32 oracle."""
+    cfg = W.GEMM_F16
+    a, b, bias = W.gemm_inputs(cfg, device=DEV, seed=0)
+    c = b2.gemm(a, b, bias, "relu", torch.float16)
+    assert b2.last_kernel() == "gemm_sm100"
+    for r0 in (0, 4096 - 64, 8192 - 128):
+        ref = O.ref_gemm(a[r0:r0 + 128].cpu(), b.cpu(), bias.cpu(), "relu", torch.float32)
+        _check(c[r0:r0 + 128], ref, torch.float16)
+
+
+# ------------------------------------------------------------------- row ops
+ROW_OPS = ["softmax", "layernorm", "rmsnorm", "sum", "max", "min", "argmax", "argmin"]
+
+
+def _row_run(op, x, w, b):
+    if op == "softmax":
+        return b2.row_softmax(x)
+    if op == "layernorm":
+        return b2.row_layernorm(x, w, b, 1e-5)
+    if op == "rmsnorm":
+        return b2.row_rmsnorm(x, w, 1e-6)
+    return getattr(b2, f"row_{op}")(x)
+
+
+def _row_ref(op, x, w, b):
+    return O.ROW_REFS[op](x, w, b, 1e-5 if op == "layernorm" else 1e-6)
+
+
+@pytest.mark.parametrize("op", ROW_OPS)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("rows,cols", [(257, 4096), (64, 1000), (33, 4097), (128, 7), (5, 1),
+                                       (16, 32768), (4, 40000), (1000, 128)])
+def test_row_ops_match_oracle(op, dtype, rows, cols):
+    x = _rand((rows, cols), dtype, rows * 7 + cols)
+    w = (1 + 0.1 * _rand((cols,), torch.float32, 3)).to(dtype)
+    b = (0.1 * _rand((cols,), torch.float32, 4)).to(dtype)
+    got = _row_run(op, x.to(DEV), w.to(DEV), b.to(DEV))
+    ref = _row_ref(op, x, w, b)
+    if op.startswith("arg"):
+        assert torch.equal(got.cpu(), ref)
+    else:
+        _check(got, ref, dtype)
+
+
+@pytest.mark.parametrize("op", ["sum", "max", "min", "argmax", "argmin"])
+def test_row_split_path_long_rows(op):
+    x = _rand((3, 1 << 20), torch.float32, 77)
+    x[1, 777777] = 9.0
+    x[1, 5] = 9.0   # tie: lower index wins
+    got = _row_run(op, x.to(DEV), None, None)
+    assert b2.last_kernel() == "row_split"
+    ref = _row_ref(op, x, None, None)
+    if op.startswith("arg"):
+        assert torch.equal(got.cpu(), ref)
+    elif op == "sum":
+        # 1M-element sums: compare against a float64 sum, relative to sum|x|
+        exact = x.double().sum(-1)
+        assert ((got.cpu().double() - exact).abs() / x.double().abs().sum(-1)).max() < 1e-6
+    else:
+        assert torch.equal(got.cpu(), ref)
+
+
+def test_row_nan_and_tie_semantics():
+    x = torch.randn(8, 300)
+    x[0, :] = 2.0
+    x[1, 10] = x[1, 200] = 99.0
+    x[2, 123] = float("nan")
+    x[3, 7] = x[3, 250] = float("nan")
+    x[4, 0] = float("-inf")
+    xd = x.to(DEV)
+    assert torch.equal(b2.row_argmax(xd).cpu(), O.ref_argmax(x))
+    assert torch.equal(b2.row_argmin(xd).cpu(), O.ref_argmin(x))
+    assert torch.allclose(b2.row_max(xd).cpu(), O.ref_max(x), equal_nan=True)
+    assert torch.allclose(b2.row_min(xd).cpu(), O.ref_min(x), equal_nan=True)
+    s = b2.row_sum(xd).cpu()
+    assert torch.isnan(s[2]) and torch.isnan(s[3])
+
+
+def test_row_edge_shapes():
+    x = torch.randn(0, 16, device=DEV)
+    assert b2.row_softmax(x).shape == (0, 16)
+    assert b2.row_sum(torch.randn(4, 0, device=DEV)).tolist() == [0, 0, 0, 0]
+    with pytest.raises(b2.B2Error):
+        b2.row_argmax(torch.randn(4, 0, device=DEV))
+    x3 = torch.randn(2, 3, 96, device=DEV)
+    assert torch.allclose(b2.row_softmax(x3).cpu(), O.ref_softmax(x3.cpu()), atol=1e-6)
+    xs = torch.randn(64, 200, device=DEV)[:, :100]      # row stride 200
+    assert torch.allclose(b2.row_rmsnorm(xs).cpu(), O.ref_rmsnorm(xs.cpu()), atol=1e-5)
+
+
+def test_row_config4_full_size_properties():
+    """BASELINE config 4 at full size: sampled rows vs the oracle, plus
+    size-independent properties over every row."""
+    x, w, b = W.row_inputs(W.ROWS_F32, device=DEV, seed=0)
+    idx = torch.tensor([0, 1, 4095, 32768, 65535])
+    xs = x[idx].cpu()
+    sm = b2.row_softmax(x)
+    assert ((sm.sum(-1) - 1).abs().max().item()) < 1e-5
+    _check(sm[idx], O.ref_softmax(xs), torch.float32)
+    ln = b2.row_layernorm(x, w, b, 1e-5)
+    _check(ln[idx], O.ref_layernorm(xs, w.cpu(), b.cpu(), 1e-5), torch.float32)
+    rn = b2.row_rmsnorm(x, w, 1e-6)
+    _check(rn[idx], O.ref_rmsnorm(xs, w.cpu(), 1e-6), torch.float32)
+    am = b2.row_argmax(x)
+    assert torch.equal(am, torch.argmax(x, dim=-1))
+    mx = b2.row_max(x)
+    assert torch.equal(mx, x.gather(1, am[:, None])[:, 0])
+    _check(b2.row_sum(x)[idx], O.ref_sum(xs), torch.float32)
+
+
+def test_device_status_clean():
+    assert b2.device_status(0) == 0

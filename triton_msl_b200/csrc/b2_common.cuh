@@ -1,0 +1,100 @@
+// Shared host/device definitions for the b2msl kernels (status codes, dtype
+// tags, per-thread error text, the device status word every bounded wait writes).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/b2msl.h"
+
+namespace b2 {
+
+// Thread-local text behind b2_last_error(); set by every failing entry point.
+void set_error(const char* fmt, ...);
+void clear_error();
+
+// Device status bits, OR-ed into a per-module __device__ word by kernels and
+// read back with b2_device_status().
+enum : uint32_t {
+  DEV_OK = 0u,
+  DEV_TIMEOUT_TMA = 1u << 0,    // a consumer waited too long for a TMA fill
+  DEV_TIMEOUT_MMA = 1u << 1,    // a waiter gave up on a tensor-core commit
+  DEV_TIMEOUT_EPI = 1u << 2,    // an epilogue/softmax waiter gave up
+  DEV_TIMEOUT_SLOT = 1u << 3,   // a producer gave up waiting for a free slot
+};
+
+// Upper bound on any single spin inside a kernel. Every legitimate wait in
+// these kernels is microseconds; one second means the pipeline is wedged.
+constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case B2_F32: return 4;
+    case B2_F16: return 2;
+    case B2_BF16: return 2;
+    case B2_I64: return 8;
+    default: return 0;
+  }
+}
+
+inline const char* dtype_name(int dt) {
+  switch (dt) {
+    case B2_F32: return "f32";
+    case B2_F16: return "f16";
+    case B2_BF16: return "bf16";
+    case B2_I64: return "i64";
+    default: return "?";
+  }
+}
+
+// Converters used by every kernel family: load any of the three float types
+// as fp32, store fp32 as any of them (round-to-nearest-even).
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Epilogue activations shared by the GEMM kernels. ReLU propagates NaN, as
+// torch.relu does (the reference's epilogue maps tl.maximum to a NaN-propagating max).
+__device__ __forceinline__ float apply_act(float x, int act) {
+  switch (act) {
+    case B2_ACT_RELU: return (x > 0.f || x != x) ? x : 0.f;
+    case B2_ACT_GELU: return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+    case B2_ACT_GELU_TANH: {
+      const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+      return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+    }
+    case B2_ACT_SILU: return x / (1.f + __expf(-x));
+    default: return x;
+  }
+}
+
+}  // namespace b2
+
+#define B2_CUDA_TRY(expr)                                                        \
+  do {                                                                           \
+    cudaError_t _e = (expr);                                                     \
+    if (_e != cudaSuccess) {                                                     \
+      ::b2::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e),    \
+                      __FILE__, __LINE__);                                       \
+      return B2_ELAUNCH;                                                         \
+    }                                                                            \
+  } while (0)
+
+#define B2_CHECK_LAUNCH()                                                        \
+  do {                                                                           \
+    cudaError_t _e = cudaGetLastError();                                         \
+    if (_e != cudaSuccess) {                                                     \
+      ::b2::set_error("kernel launch failed: %s (%s:%d)", cudaGetErrorString(_e),\
+                      __FILE__, __LINE__);                                       \
+      return B2_ELAUNCH;                                                         \
+    }                                                                            \
+  } while (0)

@@ -1,0 +1,240 @@
+// C ABI entry points (include/b2msl.h): argument validation, path selection
+// and error reporting. Validation is complete before any launch, so a failing
+// call never leaves partial work on the stream.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "b2_common.cuh"
+
+namespace b2 {
+
+// kernels (defined in the family translation units)
+int fa_simt_launch(const void*, const void*, const void*, void*, long long, long long, long long,
+                   long long, const int64_t*, float, int, int, cudaStream_t);
+bool fa_sm100_eligible(const void*, const void*, const void*, const void*, long long,
+                       const int64_t*, int);
+int fa_sm100_launch(const void*, const void*, const void*, void*, long long, long long, long long,
+                    long long, const int64_t*, float, int, int, cudaStream_t);
+int gemm_simt_launch(const void*, const void*, const void*, void*, long long, long long, long long,
+                     const int64_t*, float, int, int, int, int, cudaStream_t);
+bool gemm_sm100_eligible(const void*, const void*, long long, long long, long long,
+                         const int64_t*, int);
+int gemm_sm100_launch(const void*, const void*, const void*, void*, long long, long long,
+                      long long, const int64_t*, float, int, int, int, int, cudaStream_t);
+size_t row_op_workspace(int, long long, long long);
+int row_op_launch(int, const void*, const void*, const void*, void*, long long, long long,
+                  long long, long long, float, int, void*, size_t, cudaStream_t);
+uint32_t row_read_status(bool);
+uint32_t gemm_read_status(bool);
+uint32_t fa_read_status(bool);
+
+namespace {
+thread_local std::string t_err;
+thread_local const char* t_kernel = "";
+
+// Tensor-core kernels need an sm_100-class device; remember per device.
+constexpr int kMaxDev = 64;
+int g_cc_major[kMaxDev];
+std::once_flag g_cc_once[kMaxDev];
+
+bool device_is_sm100() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return false;
+  std::call_once(g_cc_once[dev], [dev] {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    g_cc_major[dev] = major;
+  });
+  return g_cc_major[dev] == 10;
+}
+
+bool valid_float_dtype(int dt) { return dt == B2_F32 || dt == B2_F16 || dt == B2_BF16; }
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+}
+void clear_error() { t_err.clear(); }
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+const char* b2_version(void) { return "b2msl 0.1.0 sm_100a"; }
+
+const char* b2_last_error(void) { return t_err.c_str(); }
+
+// Name of the kernel family the last successful call on this thread launched
+// (test/bench introspection; not part of the reference surface).
+const char* b2_last_kernel(void) { return t_kernel; }
+
+int b2_fa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
+              int64_t S, int64_t D, const int64_t strides[16], float sm_scale, int causal,
+              int dtype, void* stream) {
+  clear_error();
+  if (B < 0 || H < 0 || S < 0 || D <= 0) {
+    set_error("b2_fa_fwd: invalid shape B=%lld H=%lld S=%lld D=%lld", (long long)B, (long long)H,
+              (long long)S, (long long)D);
+    return B2_EINVAL;
+  }
+  if (!valid_float_dtype(dtype)) {
+    set_error("b2_fa_fwd: unsupported dtype %d", dtype);
+    return B2_EINVAL;
+  }
+  if (B == 0 || H == 0 || S == 0) return B2_OK;
+  if (!q || !k || !v || !o || !strides) {
+    set_error("b2_fa_fwd: null pointer argument");
+    return B2_EINVAL;
+  }
+  if (!(sm_scale == sm_scale) || sm_scale == INFINITY || sm_scale == -INFINITY) {
+    set_error("b2_fa_fwd: sm_scale must be finite");
+    return B2_EINVAL;
+  }
+  if (D > 128) {
+    set_error("b2_fa_fwd: head_dim %lld > 128 is not supported", (long long)D);
+    return B2_EUNSUPPORTED;
+  }
+  if (S >= (1LL << 31) || B * H >= (1LL << 31)) {
+    set_error("b2_fa_fwd: S and B*H must be < 2^31");
+    return B2_EINVAL;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  if (sm_scale > 0.f && device_is_sm100() && fa_sm100_eligible(q, k, v, o, D, strides, dtype)) {
+    rc = fa_sm100_launch(q, k, v, o, B, H, S, D, strides, sm_scale, causal ? 1 : 0, dtype, st);
+    if (rc == B2_OK) t_kernel = "fa_sm100";
+  } else {
+    rc = fa_simt_launch(q, k, v, o, B, H, S, D, strides, sm_scale, causal ? 1 : 0, dtype, st);
+    if (rc == B2_OK) t_kernel = "fa_simt";
+  }
+  return rc;
+}
+
+int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
+            int64_t K, const int64_t strides[6], float alpha, int act, int in_dtype,
+            int bias_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
+  (void)workspace;
+  (void)ws_bytes;
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) {
+    set_error("b2_gemm: invalid shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+    return B2_EINVAL;
+  }
+  if (!valid_float_dtype(in_dtype) || !valid_float_dtype(out_dtype) ||
+      (bias && !valid_float_dtype(bias_dtype))) {
+    set_error("b2_gemm: unsupported dtype combination in=%d bias=%d out=%d", in_dtype, bias_dtype,
+              out_dtype);
+    return B2_EINVAL;
+  }
+  if (act < B2_ACT_NONE || act > B2_ACT_SILU) {
+    set_error("b2_gemm: unknown activation %d", act);
+    return B2_EINVAL;
+  }
+  if (M == 0 || N == 0) return B2_OK;
+  if (!C || !strides || (K > 0 && (!A || !Bm))) {
+    set_error("b2_gemm: null pointer argument");
+    return B2_EINVAL;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  if (device_is_sm100() && strides[5] == 1 && gemm_sm100_eligible(A, Bm, M, N, K, strides, in_dtype)) {
+    rc = gemm_sm100_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
+                           out_dtype, st);
+    if (rc == B2_OK) t_kernel = "gemm_sm100";
+  } else {
+    rc = gemm_simt_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
+                          out_dtype, st);
+    if (rc == B2_OK) t_kernel = "gemm_simt";
+  }
+  return rc;
+}
+
+int b2_row_op(int op, const void* x, const void* w, const void* b, void* out, int64_t rows,
+              int64_t cols, int64_t ld_x, int64_t ld_out, float eps, int dtype, void* workspace,
+              size_t ws_bytes, void* stream) {
+  clear_error();
+  if (op < B2_ROW_SOFTMAX || op > B2_ROW_ARGMIN) {
+    set_error("b2_row_op: unknown op %d", op);
+    return B2_EINVAL;
+  }
+  if (!valid_float_dtype(dtype)) {
+    set_error("b2_row_op: unsupported dtype %d", dtype);
+    return B2_EINVAL;
+  }
+  if (rows < 0 || cols < 0) {
+    set_error("b2_row_op: invalid shape rows=%lld cols=%lld", (long long)rows, (long long)cols);
+    return B2_EINVAL;
+  }
+  const bool row_out = op == B2_ROW_SOFTMAX || op == B2_ROW_LAYERNORM || op == B2_ROW_RMSNORM;
+  if (cols == 0 && (op == B2_ROW_MAX || op == B2_ROW_MIN || op == B2_ROW_ARGMAX || op == B2_ROW_ARGMIN) && rows > 0) {
+    set_error("b2_row_op: max/min/argmax/argmin over an empty row is undefined");
+    return B2_EINVAL;
+  }
+  if (rows == 0 || (cols == 0 && row_out)) return B2_OK;
+  if (!x || !out) {
+    set_error("b2_row_op: null pointer argument");
+    return B2_EINVAL;
+  }
+  if (ld_x < cols || (row_out && ld_out < cols)) {
+    set_error("b2_row_op: row stride smaller than the row (ld_x=%lld ld_out=%lld cols=%lld)",
+              (long long)ld_x, (long long)ld_out, (long long)cols);
+    return B2_EINVAL;
+  }
+  if (rows >= (1LL << 31)) {
+    set_error("b2_row_op: rows must be < 2^31");
+    return B2_EINVAL;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cols == 0) {  // sum over an empty row is 0
+    const size_t bytes = (size_t)rows * dtype_size(dtype);
+    B2_CUDA_TRY(cudaMemsetAsync(out, 0, bytes, st));
+    t_kernel = "row_memset";
+    return B2_OK;
+  }
+  const int rc = row_op_launch(op, x, w, b, out, rows, cols, ld_x, ld_out, eps, dtype, workspace,
+                               ws_bytes, st);
+  if (rc == B2_OK) t_kernel = row_op_workspace(op, rows, cols) ? "row_split" : "row_reduce";
+  return rc;
+}
+
+size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3) {
+  (void)a3;
+  switch (kind) {
+    case 0: return 0;
+    case 1: return row_op_workspace((int)a0, a1, a2);
+    case 2: return 0;
+    default: return 0;
+  }
+}
+
+int b2_device_status(int device, int clear, uint32_t* status_out) {
+  clear_error();
+  int prev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&prev));
+  B2_CUDA_TRY(cudaSetDevice(device));
+  cudaError_t e = cudaDeviceSynchronize();
+  uint32_t s = 0;
+  if (e == cudaSuccess) {
+    s |= row_read_status(clear != 0);
+    s |= gemm_read_status(clear != 0);
+    s |= fa_read_status(clear != 0);
+    e = cudaGetLastError();
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_error("b2_device_status: %s", cudaGetErrorString(e));
+    return B2_ELAUNCH;
+  }
+  if (status_out) *status_out = s;
+  return s ? B2_ETIMEOUT : B2_OK;
+}
+
+}  // extern "C"

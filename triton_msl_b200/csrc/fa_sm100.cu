@@ -1,0 +1,431 @@
+// FlashAttention forward on 5th-generation tensor cores (fp16 / bf16 in,
+// fp32 accumulate), head_dim 32, 64 or 128.
+//
+// Replaces the reference's simdgroup-MMA template
+// `make_flash_attention_kernel_simdgroup` (triton_msl/codegen/_msl_templates.py:1833-2070),
+// with the semantics of the canonical kernel `_flash_attn_fwd`
+// (tests/test_flash_attention.py:35-118): online max / exp / sum per block of
+// keys, causal keep iff key <= query with the key loop bounded by the query
+// block, O / l at the end.
+//
+// One CTA owns 256 query rows (two 128-row tiles Q0, Q1) of one (batch, head):
+//  * warp 0: TMA producer (Q0, Q1 once; K_j, V_j through 2-deep rings).
+//  * warp 1: TMEM allocation and the single issuing thread of tcgen05.mma.
+//  * warps 4-7: softmax + O correction for Q0; warps 8-11: the same for Q1.
+// TMEM (512 columns): S0 | S1 (128 fp32 columns each) | O0 | O1 (D each).
+// The softmax warps read S_t row-per-thread, write P_t as packed fp16/bf16
+// over the first 64 columns of S_t, and the MMA warp consumes P_t straight
+// from TMEM (tcgen05.mma with A in tensor memory), so P never touches shared
+// memory. MMA issue order per key block j:
+//     PV0_j, S0_{j+1}, PV1_j, S1_{j+1}
+// so while one softmax warpgroup works on S_t the tensor core runs the other
+// tile's GEMMs. A commit after S_t_{j+1} also covers PV_t_j (commits track all
+// earlier MMAs), which is what lets the softmax warps rescale O_t safely.
+// O is only rescaled when a row max grows by more than 2^8 (the stale max is
+// used consistently for P and l, so the result is exact up to rounding).
+#include "sm100.cuh"
+
+namespace b2 {
+namespace {
+
+using namespace sm100;
+
+__device__ uint32_t g_fa_status;
+
+constexpr int kBM = 128;      // query rows per tile
+constexpr int kBN = 128;      // keys per block
+constexpr int kThreads = 384; // 12 warps
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct __align__(8) FaBarriers {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full;
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int D>
+struct FaCfg {
+  static constexpr int kAtom = D >= 64 ? 64 : 32;           // elements per swizzle atom row
+  static constexpr int kAtomBytes = kAtom * 2;              // 128 or 64
+  static constexpr uint32_t kSwz = D >= 64 ? kSwizzle128 : kSwizzle64;
+  static constexpr int kNumAtoms = D / kAtom;
+  static constexpr uint32_t kTileBytes = 128 * D * 2;       // one 128-row tile
+  static constexpr uint32_t kAtomTileBytes = 128 * kAtomBytes;
+  static constexpr uint32_t kSBO = 8 * kAtomBytes;          // 8-row group pitch
+  static constexpr size_t kSmem = 1024 + 6 * kTileBytes + sizeof(FaBarriers);
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int H, int S,
+                int num_qblk, long long soz, long long soh, long long som, float scale_log2,
+                int causal) {
+  using Cfg = FaCfg<D>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                              // 2 tiles
+  uint8_t* sK = smem + 2 * Cfg::kTileBytes;        // 2 stages
+  uint8_t* sV = smem + 4 * Cfg::kTileBytes;        // 2 stages
+  FaBarriers* bars = reinterpret_cast<FaBarriers*>(smem + 6 * Cfg::kTileBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = gridDim.x / num_qblk;
+  // Heaviest query blocks first (causal work grows with the block index).
+  const int qblk = num_qblk - 1 - (int)(blockIdx.x / BH);
+  const int bh = blockIdx.x % BH;
+  const int b = bh / H, h = bh % H;
+  const int m0 = qblk * 2 * kBM;
+  const int nkv_all = (S + kBN - 1) / kBN;
+  int n1 = nkv_all, n0 = nkv_all;  // key blocks for Q1 / Q0
+  if (causal) {
+    n1 = min((m0 + 2 * kBM + kBN - 1) / kBN, nkv_all);
+    n0 = min((m0 + kBM + kBN - 1) / kBN, nkv_all);
+  }
+  const int n = n1;  // K/V blocks streamed
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);
+    }
+    mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t k_filled = 0, v_filled = 0;
+      mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int a = 0; a < Cfg::kNumAtoms; ++a)
+          tma_load_4d(sQ + t * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmQ, &bars->q_full,
+                      a * Cfg::kAtom, m0 + t * kBM, h, b);
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1u;
+        if (!mbar_wait(&bars->k_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars->k_full[s], Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kNumAtoms; ++a)
+          tma_load_4d(sK + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmK, &bars->k_full[s],
+                      a * Cfg::kAtom, j * kBN, h, b);
+        k_filled = j + 1;
+        if (!mbar_wait(&bars->v_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars->v_full[s], Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kNumAtoms; ++a)
+          tma_load_4d(sV + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmV, &bars->v_full[s],
+                      a * Cfg::kAtom, j * kBN, h, b);
+        v_filled = j + 1;
+      }
+      // Bounded drain of copies still in flight into this CTA's shared memory.
+      const unsigned long long t0 = globaltimer();
+      auto drain = [&](uint64_t* bar, uint32_t par) {
+        while (!mbar_test(smem_addr(bar), par)) {
+          if (globaltimer() - t0 > kWaitLimitNs) { atomicOr(&g_fa_status, DEV_TIMEOUT_TMA); return; }
+        }
+      };
+      drain(&bars->q_full, 0);
+      for (uint32_t j = (k_filled > 2 ? k_filled - 2 : 0); j < k_filled; ++j) drain(&bars->k_full[j & 1], (j >> 1) & 1);
+      for (uint32_t j = (v_filled > 2 ? v_filled - 2 : 0); j < v_filled; ++j) drain(&bars->v_full[j & 1], (j >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_f16(kBM, kBN, BF16, false, false);  // Q K^T: both K-major
+      constexpr uint32_t idO = idesc_f16(kBM, D, BF16, false, true);     // P V: V is MN-major
+      const uint32_t q0 = smem_addr(sQ), k0 = smem_addr(sK), v0 = smem_addr(sV);
+      bool ok = true;
+      bool issued = false;
+      auto qk = [&](int t, int ks) {
+        const uint32_t qa = q0 + t * Cfg::kTileBytes, ka = k0 + ks * Cfg::kTileBytes;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k * 16 / Cfg::kAtom) * Cfg::kAtomTileBytes + (k * 16 % Cfg::kAtom) * 2;
+          mma_f16_ss(tS[t], sdesc(qa + off, 16, Cfg::kSBO, Cfg::kSwz),
+                     sdesc(ka + off, 16, Cfg::kSBO, Cfg::kSwz), idS, k > 0 ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int t, int vs, bool accumulate) {
+        const uint32_t va = v0 + vs * Cfg::kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          // A = P_t: 16 keys = 8 packed TMEM columns per step.
+          // B = V: MN-major, 16 key rows = 16 * atom-row bytes per step,
+          //        64-wide D chunks kAtomTileBytes apart.
+          mma_f16_ts(tO[t], tS[t] + k * 8,
+                     sdesc(va + k * 16 * Cfg::kAtomBytes, Cfg::kAtomTileBytes, Cfg::kSBO, Cfg::kSwz),
+                     idO, (accumulate || k > 0) ? 1u : 0u);
+        }
+      };
+      do {
+        if (!mbar_wait(&bars->q_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+        if (!mbar_wait(&bars->k_full[0], 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+        tc_fence_after();
+        if (n0 > 0) { qk(0, 0); mma_commit(&bars->s_full[0]); }
+        qk(1, 0);
+        mma_commit(&bars->s_full[1]);
+        mma_commit(&bars->k_empty[0]);
+        issued = true;
+        for (int j = 0; j < n; ++j) {
+          const int vs = j & 1;
+          const uint32_t vph = (j >> 1) & 1;
+          if (!mbar_wait(&bars->v_full[vs], vph, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+          if (j < n0) {
+            if (!mbar_wait(&bars->p_full[0], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
+            tc_fence_after();
+            pv(0, vs, j > 0);
+          }
+          const int ks = (j + 1) & 1;
+          if (j + 1 < n) {
+            if (!mbar_wait(&bars->k_full[ks], ((j + 1) >> 1) & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+            tc_fence_after();
+            if (j + 1 < n0) { qk(0, ks); mma_commit(&bars->s_full[0]); }
+          }
+          if (!mbar_wait(&bars->p_full[1], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
+          tc_fence_after();
+          pv(1, vs, j > 0);
+          mma_commit(&bars->v_empty[vs]);
+          if (j + 1 < n) {
+            qk(1, ks);
+            mma_commit(&bars->s_full[1]);
+            mma_commit(&bars->k_empty[ks]);
+          }
+        }
+        if (ok) mma_commit(&bars->o_full);
+      } while (false);
+      if (issued) {
+        mma_commit(&bars->done);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_test(smem_addr(&bars->done), 0)) {
+          if (globaltimer() - t0 > kWaitLimitNs) { atomicOr(&g_fa_status, DEV_TIMEOUT_MMA); break; }
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------- softmax / correction
+    const int t = (warp >= 8) ? 1 : 0;
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const int qrow = m0 + t * kBM + row_in_tile;
+    const int n_t = t == 0 ? n0 : n1;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m_run = -INFINITY;  // running max in log2 units (possibly stale)
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_t; ++j) {
+      if (!mbar_wait(&bars->s_full[t], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) { ok = false; break; }
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS[t] + lane_off + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int kbase = j * kBN;
+      const bool need_mask = (kbase + kBN > S) || (causal && kbase + kBN - 1 > m0 + t * kBM);
+      float mx = -INFINITY;
+      if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i) {
+          const int key = kbase + i;
+          if (key >= S || (causal && key > qrow)) s[i] = -INFINITY;
+          mx = fmaxf(mx, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i) mx = fmaxf(mx, s[i]);
+      }
+      mx *= scale_log2;
+      // Rescale only when some row of this warp grew its max by > 2^8.
+      const bool grow = mx > m_run + kRescaleThreshold;
+      const bool warp_rescale = __any_sync(0xffffffffu, grow);
+      float alpha = 1.f;
+      if (warp_rescale) {
+        const float m_new = fmaxf(m_run, mx);
+        alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      float rowsum = 0.f;
+      uint32_t p[kBN / 2];
+#pragma unroll
+      for (int i = 0; i < kBN / 2; ++i) {
+        const float p0 = ex2(fmaf(s[2 * i], scale_log2, -m_use));
+        const float p1 = ex2(fmaf(s[2 * i + 1], scale_log2, -m_use));
+        rowsum += p0 + p1;
+        p[i] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+      }
+      l_run = l_run * alpha + rowsum;
+#pragma unroll
+      for (int c = 0; c < kBN / 2 / 32; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = p[c * 32 + i];
+        tmem_st32(tS[t] + lane_off + c * 32, r);
+      }
+      if (warp_rescale && j > 0) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO[t] + lane_off + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO[t] + lane_off + c * 32, r);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[t]);
+    }
+    if (ok && mbar_wait(&bars->o_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T* orow = reinterpret_cast<T*>(out) + (long long)b * soz + (long long)h * soh + (long long)qrow * som;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tO[t] + lane_off + c * 32, r);
+        tmem_ld_wait();
+        if (qrow < S) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 u;
+            u.x = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 0]) * inv, __uint_as_float(r[v * 8 + 1]) * inv)
+                       : pack_half2(__uint_as_float(r[v * 8 + 0]) * inv, __uint_as_float(r[v * 8 + 1]) * inv);
+            u.y = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv)
+                       : pack_half2(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv);
+            u.z = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv)
+                       : pack_half2(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv);
+            u.w = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv)
+                       : pack_half2(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv);
+            dst[v] = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int launch(const void* q, const void* k, const void* v, void* o, long long B, long long H,
+           long long S, const int64_t* s, float sm_scale, int causal, cudaStream_t st) {
+  using Cfg = FaCfg<D>;
+  const CUtensorMapDataType tdt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapSwizzle swz = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap tm[3];
+  const void* ptrs[3] = {q, k, v};
+  for (int i = 0; i < 3; ++i) {
+    const int64_t* st4 = s + 4 * i;  // z, h, m, d strides
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)st4[2] * 2, (uint64_t)st4[1] * 2, (uint64_t)st4[0] * 2};
+    const uint32_t box[4] = {(uint32_t)Cfg::kAtom, 128, 1, 1};
+    if (!encode_tmap(&tm[i], tdt, 4, ptrs[i], dims, strides, box, swz)) return B2_ELAUNCH;
+  }
+  auto kern = fa_sm100_kernel<D, BF16>;
+  B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem));
+  const int num_qblk = (int)((S + 2 * kBM - 1) / (2 * kBM));
+  const long long grid = (long long)num_qblk * B * H;
+  if (grid >= (1LL << 31)) {
+    set_error("b2_fa_fwd: grid too large");
+    return B2_EINVAL;
+  }
+  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, st>>>(tm[0], tm[1], tm[2], o, (int)H, (int)S, num_qblk,
+                                                      s[12], s[13], s[14], sm_scale * kLog2e, causal);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+}  // namespace
+
+bool fa_sm100_eligible(const void* q, const void* k, const void* v, const void* o, long long D,
+                       const int64_t* s, int dtype) {
+  if (dtype != B2_F16 && dtype != B2_BF16) return false;
+  if (D != 32 && D != 64 && D != 128) return false;
+  const void* p[4] = {q, k, v, o};
+  for (int i = 0; i < 4; ++i) {
+    if ((reinterpret_cast<uintptr_t>(p[i]) & 15) != 0) return false;
+    if (s[4 * i + 3] != 1) return false;
+    for (int j = 0; j < 3; ++j)
+      if ((s[4 * i + j] * 2) % 16 != 0) return false;
+  }
+  return true;
+}
+
+int fa_sm100_launch(const void* q, const void* k, const void* v, void* o, long long B, long long H,
+                    long long S, long long D, const int64_t* s, float sm_scale, int causal,
+                    int dtype, cudaStream_t st) {
+  const bool bf = dtype == B2_BF16;
+  switch (D) {
+    case 32: return bf ? launch<32, true>(q, k, v, o, B, H, S, s, sm_scale, causal, st)
+                       : launch<32, false>(q, k, v, o, B, H, S, s, sm_scale, causal, st);
+    case 64: return bf ? launch<64, true>(q, k, v, o, B, H, S, s, sm_scale, causal, st)
+                       : launch<64, false>(q, k, v, o, B, H, S, s, sm_scale, causal, st);
+    case 128: return bf ? launch<128, true>(q, k, v, o, B, H, S, s, sm_scale, causal, st)
+                        : launch<128, false>(q, k, v, o, B, H, S, s, sm_scale, causal, st);
+  }
+  set_error("b2_fa_fwd: tensor-core path supports head_dim 32/64/128, got %lld", D);
+  return B2_EUNSUPPORTED;
+}
+
+uint32_t fa_read_status(bool clear) {
+  uint32_t v = 0;
+  cudaMemcpyFromSymbol(&v, g_fa_status, sizeof(v));
+  if (clear) {
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(g_fa_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace b2

@@ -1,0 +1,377 @@
+// GEMM with fused bias/activation epilogue on 5th-generation tensor cores.
+//
+// Replaces the reference's fast matmul (`make_simdgroup_matmul_kernel_fast`,
+// triton_msl/codegen/_msl_templates.py:4134-4255: fp32 accumulate, cast out)
+// and its staged epilogue (`_lower_matmul_softmax_template` /
+// `_emit_matmul_epilogue_loop`, _lowerer_templates.py:1515-1855: column bias
+// folded into the accumulator, then the activation, then the store). The
+// reference refuses a K-looped matmul with an epilogue; here the epilogue is
+// fused into every tile.
+//
+// Design (one CTA per SM, persistent):
+//  * C tile 128 x 256, K step 64 (one 128-byte swizzle atom), 4-stage
+//    TMA -> shared-memory ring (48 KB per stage).
+//  * warp 0: TMA producer; warp 1: TMEM allocation + single-thread tcgen05.mma
+//    issue (M=128, N=256, K=16 per instruction); warps 2-5: epilogue.
+//  * Two 256-column fp32 accumulators in TMEM (all 512 columns), so the
+//    epilogue of tile i overlaps the main loop of tile i+1.
+//  * A is K-major ([M,K] row-major). B is either MN-major ([K,N] row-major, the
+//    reference `A @ B` layout) or K-major ([N,K] row-major, `x @ w.t()`); the
+//    instruction descriptor's B-major bit selects it, no transpose pass.
+//  * Epilogue: tcgen05.ld 32 columns at a time, alpha, + bias[n], activation,
+//    convert, 16-byte stores.
+//  * Every mbarrier wait is bounded (see sm100.cuh).
+#include "sm100.cuh"
+
+namespace b2 {
+namespace {
+
+using namespace sm100;
+
+__device__ uint32_t g_gemm_status;
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr int kGroupM = 16;                    // raster: 16 M-tiles per group
+constexpr uint32_t kTmemCols = 512;
+
+struct __align__(8) GemmBarriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ float bias_at(const void* b, int dt, int n) {
+  if (dt == B2_F32) return __ldg(reinterpret_cast<const float*>(b) + n);
+  if (dt == B2_F16) return __half2float(reinterpret_cast<const __half*>(b)[n]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(b)[n]);
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(num_m - first_m, kGroupM);
+  const int r = t % per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+template <typename TO, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
+                  int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kABytes;
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + kStages * kStageBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
+  const int tiles = num_m * num_n;
+  const int nk = (K + kBK - 1) / kBK;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 4);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled = 0;  // stages filled at least once
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_SLOT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
+          tma_load_2d(sA + stage * kABytes, &tmA, &bars->full[stage], kb * kBK, mb * kBM);
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < kBN / 64; ++j)
+              tma_load_2d(sB + stage * kBBytes + j * (64 * kBK * 2), &tmB, &bars->full[stage],
+                          nb * kBN + j * 64, kb * kBK);
+          } else {
+            tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], kb * kBK, nb * kBN);
+          }
+          filled |= 1u << stage;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave with bulk copies in flight into this CTA's shared memory:
+      // wait (bounded) for the latest fill of every stage to land.
+      for (int s = 0; s < kStages; ++s) {
+        if (!(filled & (1u << s))) continue;
+        // the latest fill of stage s used parity (phase of that round)
+        const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_test(smem_addr(&bars->full[s]), par)) {
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicOr(&g_gemm_status, DEV_TIMEOUT_TMA);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_EPI)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kBN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sA + stage * kABytes);
+          const uint32_t b0 = smem_addr(sB + stage * kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sdesc(a0 + k * 32, 16, 1024, kSwizzle128);
+            const uint64_t bd = B_MN ? sdesc(b0 + k * 16 * 128, 64 * kBK * 2, 1024, kSwizzle128)
+                                     : sdesc(b0 + k * 32, 16, 1024, kSwizzle128);
+            mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit(&bars->empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&bars->acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: all MMAs issued by this thread have retired before TMEM is freed.
+      if (issued) {
+        mma_commit(&bars->done);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_test(smem_addr(&bars->done), 0)) {
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicOr(&g_gemm_status, DEV_TIMEOUT_MMA);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      if (!mbar_wait(&bars->acc_full[acc], acc_phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_MMA)) break;
+      tc_fence_after();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
+      TO* crow = C + (long long)row * ldc;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        tmem_ld_wait();
+        const int n0 = nb * kBN + c * 32;
+        if (row >= M || n0 >= N) continue;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(r[j]) * alpha;
+          if (bias != nullptr && n0 + j < N) x += bias_at(bias, bias_dt, n0 + j);
+          f[j] = apply_act(x, act);
+        }
+        if (vec_ok && n0 + 32 <= N) {
+          if constexpr (sizeof(TO) == 2) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + n0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 u;
+              TO* h = reinterpret_cast<TO*>(&u);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) h[j] = from_f32<TO>(f[v * 8 + j]);
+              dst[v] = u;
+            }
+          } else {
+            float4* dst = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(f[v * 4], f[v * 4 + 1], f[v * 4 + 2], f[v * 4 + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) crow[n0 + j] = from_f32<TO>(f[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int g_sms = 0;
+
+template <typename TO, bool B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const void* bias, int bias_dt, void* C,
+           long long M, long long N, long long K, long long ldc, float alpha, int act,
+           uint32_t idesc, int vec_ok, cudaStream_t st) {
+  auto kern = gemm_sm100_kernel<TO, B_MN>;
+  const size_t smem = 1024 + kStages * kStageBytes + sizeof(GemmBarriers);
+  B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (g_sms == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const long long tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int grid = (int)(tiles < g_sms ? tiles : g_sms);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
+                                      alpha, act, idesc, vec_ok);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+}  // namespace
+
+// True when the tensor-core path can describe these operands with TMA.
+bool gemm_sm100_eligible(const void* A, const void* B, long long M, long long N, long long K,
+                         const int64_t* s, int in_dt) {
+  if (in_dt != B2_F16 && in_dt != B2_BF16) return false;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) return false;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(A) || !al16(B)) return false;
+  // A: unit K stride, row pitch a multiple of 16 bytes
+  if (s[1] != 1 || (s[0] * 2) % 16 != 0 || s[0] < K) return false;
+  const bool b_mn = s[3] == 1, b_k = s[2] == 1;
+  if (b_mn && (s[2] * 2) % 16 == 0 && s[2] >= N) return true;
+  if (b_k && (s[3] * 2) % 16 == 0 && s[3] >= K) return true;
+  return false;
+}
+
+int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, long long M,
+                      long long N, long long K, const int64_t* s, float alpha, int act, int in_dt,
+                      int bias_dt, int out_dt, cudaStream_t st) {
+  const CUtensorMapDataType tdt =
+      in_dt == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)s[0] * 2};
+    const uint32_t box[2] = {kBK, kBM};
+    if (!encode_tmap(&ta, tdt, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
+  }
+  const bool b_mn = s[3] == 1 && (s[2] * 2) % 16 == 0 && s[2] >= N;
+  if (b_mn) {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)s[2] * 2};
+    const uint32_t box[2] = {64, kBK};
+    if (!encode_tmap(&tb, tdt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
+  } else {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)s[3] * 2};
+    const uint32_t box[2] = {kBK, kBN};
+    if (!encode_tmap(&tb, tdt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
+  }
+  const uint32_t idesc = idesc_f16(kBM, kBN, in_dt == B2_BF16, false, b_mn);
+  const int osz = dtype_size(out_dt);
+  const int vec_ok = s[5] == 1 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
+  if (s[5] != 1) {
+    set_error("b2_gemm: tensor-core path needs unit column stride in C");
+    return B2_EUNSUPPORTED;
+  }
+  if (bias == nullptr) bias_dt = B2_F32;
+  switch (out_dt) {
+    case B2_F16:
+      return b_mn ? launch<__half, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<__half, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+    case B2_BF16:
+      return b_mn ? launch<__nv_bfloat16, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<__nv_bfloat16, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+    case B2_F32:
+      return b_mn ? launch<float, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<float, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+  }
+  set_error("b2_gemm: unsupported out dtype %d", out_dt);
+  return B2_EINVAL;
+}
+
+uint32_t gemm_read_status(bool clear) {
+  uint32_t v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v));
+  if (clear) {
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace b2

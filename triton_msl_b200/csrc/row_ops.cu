@@ -1,0 +1,644 @@
+// Row-reduction family for sm_100a: softmax, LayerNorm, RMSNorm, sum, max,
+// min, argmax, argmin over x[rows, cols].
+//
+// Reference semantics (triton-msl):
+//   softmax      _lowerer_templates.py:992-1167 (exp(x - max) / sum), prebuilt
+//                make_softmax_kernel _msl_templates.py:365-449
+//   LayerNorm    make_layer_norm_kernel _msl_templates.py:1010-1090 (two-pass
+//                mean / variance, * gamma + beta)
+//   RMSNorm      make_rms_norm_kernel _msl_templates.py:888-951
+//                (x * rsqrt(mean(x^2) + eps) * w)
+//   sum/max      make_row_reduce_kernel _msl_templates.py:259-310 and the
+//                NaN-propagating tt.reduce lowering _lowerer_reduce.py:773-1010
+//   argmax       _lowerer_reduce.py:1223-1333 (ties -> lower index)
+//
+// B200 design: HBM-bound, so each row is read exactly once with 16-byte
+// streaming loads into registers (up to 32 elements per thread), reduced with
+// warp shuffles (+ one shared-memory hop across warps), and written once with
+// 16-byte streaming stores. Rows up to 32768 fp32 (65536 fp16) stay register
+// resident. Longer or unaligned rows take a strided path that re-reads the row
+// (second read mostly hits L2). Few-but-long rows for the scalar reductions are
+// split across CTAs, with partials in caller-provided workspace.
+#include "b2_common.cuh"
+
+#include <cfloat>
+
+namespace b2 {
+namespace {
+
+__device__ uint32_t g_row_status;
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- combiners
+__device__ __forceinline__ float nan_max(float a, float b) {
+  return (a > b || a != a) ? a : b;
+}
+__device__ __forceinline__ float nan_min(float a, float b) {
+  return (a < b || a != a) ? a : b;
+}
+// true if (a, ia) beats (b, ib) for argmax (MAXI) / argmin (!MAXI): NaN is the
+// extreme value, ties and NaN-vs-NaN go to the lower index (torch semantics).
+template <bool MAXI>
+__device__ __forceinline__ bool arg_better(float a, long long ia, float b, long long ib) {
+  const bool an = a != a, bn = b != b;
+  if (an || bn) return an && (!bn || ia < ib);
+  if (MAXI) return a > b || (a == b && ia < ib);
+  return a < b || (a == b && ia < ib);
+}
+
+// ------------------------------------------------------- group reductions
+// Reductions over a group of G consecutive lanes (G <= 32) inside a warp.
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o, G);
+  return v;
+}
+template <int G>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v = nan_max(v, __shfl_xor_sync(0xffffffffu, v, o, G));
+  return v;
+}
+template <int G>
+__device__ __forceinline__ float group_min(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v = nan_min(v, __shfl_xor_sync(0xffffffffu, v, o, G));
+  return v;
+}
+template <int G, bool MAXI>
+__device__ __forceinline__ void group_arg(float& v, long long& i) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o, G);
+    long long oi = __shfl_xor_sync(0xffffffffu, i, o, G);
+    if (arg_better<MAXI>(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
+enum RedKind { RK_SUM, RK_MAX, RK_MIN };
+
+// Reduce across a row handled by TPR threads. TPR <= 32: pure shuffles inside
+// the lane group. TPR > 32: the block is one row; shuffles then one smem hop.
+template <int TPR, int KIND>
+__device__ __forceinline__ float row_reduce(float v, float* red_smem) {
+  auto op_warp = [](float x) {
+    if (KIND == RK_SUM) return group_sum<(TPR < 32 ? TPR : 32)>(x);
+    if (KIND == RK_MAX) return group_max<(TPR < 32 ? TPR : 32)>(x);
+    return group_min<(TPR < 32 ? TPR : 32)>(x);
+  };
+  v = op_warp(v);
+  if constexpr (TPR > 32) {
+    constexpr int NW = TPR / 32;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    __syncthreads();  // red_smem may still be read by a previous reduction
+    if (lane == 0) red_smem[wid] = v;
+    __syncthreads();
+    float t = lane < NW ? red_smem[lane] : (KIND == RK_SUM ? 0.f : red_smem[0]);
+    if (KIND == RK_SUM) t = group_sum<32>(t);
+    else if (KIND == RK_MAX) t = group_max<32>(t);
+    else t = group_min<32>(t);
+    v = t;
+  }
+  return v;
+}
+
+template <int TPR, bool MAXI>
+__device__ __forceinline__ void row_reduce_arg(float& v, long long& i, float* red_v, long long* red_i) {
+  group_arg<(TPR < 32 ? TPR : 32), MAXI>(v, i);
+  if constexpr (TPR > 32) {
+    constexpr int NW = TPR / 32;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { red_v[wid] = v; red_i[wid] = i; }
+    __syncthreads();
+    float tv = lane < NW ? red_v[lane] : red_v[0];
+    long long ti = lane < NW ? red_i[lane] : red_i[0];
+    group_arg<32, MAXI>(tv, ti);
+    v = tv; i = ti;
+  }
+}
+
+// -------------------------------------------------------- vector load/store
+template <typename T> struct Vec;  // 16-byte vectors of T
+template <> struct Vec<float> { static constexpr int N = 4; };
+template <> struct Vec<__half> { static constexpr int N = 8; };
+template <> struct Vec<__nv_bfloat16> { static constexpr int N = 8; };
+
+template <typename T>
+__device__ __forceinline__ void ld_vec(const T* p, float* f) {
+  const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p));
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = to_f32<T>(h[j]);
+  }
+}
+// Parameters (gamma/beta/weight) are re-read by every row: keep them cached.
+template <typename T>
+__device__ __forceinline__ void ld_vec_cached(const T* p, float* f) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = to_f32<T>(h[j]);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st_vec(T* p, const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    u.x = __float_as_uint(f[0]); u.y = __float_as_uint(f[1]);
+    u.z = __float_as_uint(f[2]); u.w = __float_as_uint(f[3]);
+  } else {
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = from_f32<T>(f[j]);
+  }
+  __stcs(reinterpret_cast<uint4*>(p), u);
+}
+
+// ------------------------------------------------- register-resident kernel
+// TPR threads per row, VPT 16-byte vectors per thread, block = max(TPR, 256)
+// threads (several rows per block when TPR < 256... only for TPR <= 32).
+// Requires cols % Vec<T>::N == 0, 16-byte aligned rows, cols <= TPR*VPT*EPV.
+template <typename T, int OP, int TPR, int VPT>
+__global__ void __launch_bounds__(TPR > 32 ? TPR : 256)
+row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bvec,
+               void* __restrict__ out, long long rows, int cols, long long ldx, long long ldo,
+               float eps) {
+  constexpr int EPV = Vec<T>::N;
+  constexpr int BLOCK = TPR > 32 ? TPR : 256;
+  constexpr int RPB = BLOCK / TPR;  // rows per block
+  static_assert(TPR <= 32 || RPB == 1, "multi-row blocks need TPR <= 32");
+  __shared__ float red_v[32];
+  __shared__ long long red_i[32];
+
+  const int sub = threadIdx.x % TPR;          // thread index inside the row
+  const int rloc = threadIdx.x / TPR;         // row slot inside the block
+  const float inv_cols = 1.f / (float)cols;
+
+  for (long long row0 = (long long)blockIdx.x * RPB; row0 < rows; row0 += (long long)gridDim.x * RPB) {
+    const long long row = row0 + rloc;
+    const bool row_ok = row < rows;
+    const T* xr = x + (row_ok ? row : 0) * ldx;
+    float v[VPT][EPV];
+    bool ok[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (sub + i * TPR) * EPV;
+      ok[i] = row_ok && c < cols;
+      if (ok[i]) ld_vec<T>(xr + c, v[i]);
+    }
+
+    if constexpr (OP == B2_ROW_SUM || OP == B2_ROW_MAX || OP == B2_ROW_MIN) {
+      float a = OP == B2_ROW_SUM ? 0.f : (OP == B2_ROW_MAX ? -INFINITY : INFINITY);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            if (OP == B2_ROW_SUM) a += v[i][j];
+            else if (OP == B2_ROW_MAX) a = nan_max(a, v[i][j]);
+            else a = nan_min(a, v[i][j]);
+          }
+        }
+      a = row_reduce<TPR, OP == B2_ROW_SUM ? RK_SUM : (OP == B2_ROW_MAX ? RK_MAX : RK_MIN)>(a, red_v);
+      if (row_ok && sub == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
+    } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+      constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+      float bv = MAXI ? -INFINITY : INFINITY;
+      long long bi = 0x7fffffffffffffffLL;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            const long long ci = (long long)(sub + i * TPR) * EPV + j;
+            if (arg_better<MAXI>(v[i][j], ci, bv, bi)) { bv = v[i][j]; bi = ci; }
+          }
+        }
+      if constexpr (TPR > 32) __syncthreads();
+      row_reduce_arg<TPR, MAXI>(bv, bi, red_v, red_i);
+      if (row_ok && sub == 0) reinterpret_cast<long long*>(out)[row] = bi;
+      if constexpr (TPR > 32) __syncthreads();
+    } else if constexpr (OP == B2_ROW_SOFTMAX) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) m = nan_max(m, v[i][j]);
+        }
+      m = row_reduce<TPR, RK_MAX>(m, red_v);
+      const float ms = m * kLog2e;
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            v[i][j] = exp2f(fmaf(v[i][j], kLog2e, -ms));
+            s += v[i][j];
+          }
+        }
+      s = row_reduce<TPR, RK_SUM>(s, red_v);
+      const float inv = 1.f / s;
+      T* o = reinterpret_cast<T*>(out) + (row_ok ? row : 0) * ldo;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[i][j] *= inv;
+          st_vec<T>(o + (sub + i * TPR) * EPV, v[i]);
+        }
+    } else if constexpr (OP == B2_ROW_LAYERNORM) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) s += v[i][j];
+        }
+      const float mean = row_reduce<TPR, RK_SUM>(s, red_v) * inv_cols;
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            const float d = v[i][j] - mean;
+            q = fmaf(d, d, q);
+          }
+        }
+      const float var = row_reduce<TPR, RK_SUM>(q, red_v) * inv_cols;
+      const float rstd = rsqrtf(var + eps);
+      T* o = reinterpret_cast<T*>(out) + (row_ok ? row : 0) * ldo;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+          const int c = (sub + i * TPR) * EPV;
+          float g[EPV], bb[EPV];
+          if (w) ld_vec_cached<T>(w + c, g);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) g[j] = 1.f;
+          }
+          if (bvec) ld_vec_cached<T>(bvec + c, bb);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) bb[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[i][j] = fmaf((v[i][j] - mean) * rstd, g[j], bb[j]);
+          st_vec<T>(o + c, v[i]);
+        }
+    } else if constexpr (OP == B2_ROW_RMSNORM) {
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) q = fmaf(v[i][j], v[i][j], q);
+        }
+      const float ms = row_reduce<TPR, RK_SUM>(q, red_v) * inv_cols;
+      const float r = rsqrtf(ms + eps);
+      T* o = reinterpret_cast<T*>(out) + (row_ok ? row : 0) * ldo;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if (ok[i]) {
+          const int c = (sub + i * TPR) * EPV;
+          float g[EPV];
+          if (w) ld_vec_cached<T>(w + c, g);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) g[j] = 1.f;
+          }
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[i][j] = v[i][j] * r * g[j];
+          st_vec<T>(o + c, v[i]);
+        }
+    }
+  }
+}
+
+// ------------------------------------------------------------ strided kernel
+// Any cols / alignment: one row per block, scalar loads, the row is re-read
+// once per pass.
+template <typename T, int OP>
+__global__ void __launch_bounds__(512)
+row_generic_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bvec,
+                   void* __restrict__ out, long long rows, long long cols, long long ldx,
+                   long long ldo, float eps) {
+  constexpr int TPR = 512;
+  __shared__ float red_v[32];
+  __shared__ long long red_i[32];
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* xr = x + row * ldx;
+    if constexpr (OP == B2_ROW_SUM || OP == B2_ROW_MAX || OP == B2_ROW_MIN) {
+      float a = OP == B2_ROW_SUM ? 0.f : (OP == B2_ROW_MAX ? -INFINITY : INFINITY);
+      for (long long c = threadIdx.x; c < cols; c += TPR) {
+        const float t = to_f32<T>(xr[c]);
+        if (OP == B2_ROW_SUM) a += t;
+        else if (OP == B2_ROW_MAX) a = nan_max(a, t);
+        else a = nan_min(a, t);
+      }
+      a = row_reduce<TPR, OP == B2_ROW_SUM ? RK_SUM : (OP == B2_ROW_MAX ? RK_MAX : RK_MIN)>(a, red_v);
+      if (threadIdx.x == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
+    } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+      constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+      float bv = MAXI ? -INFINITY : INFINITY;
+      long long bi = 0x7fffffffffffffffLL;
+      for (long long c = threadIdx.x; c < cols; c += TPR) {
+        const float t = to_f32<T>(xr[c]);
+        if (arg_better<MAXI>(t, c, bv, bi)) { bv = t; bi = c; }
+      }
+      __syncthreads();
+      row_reduce_arg<TPR, MAXI>(bv, bi, red_v, red_i);
+      if (threadIdx.x == 0) reinterpret_cast<long long*>(out)[row] = bi;
+      __syncthreads();
+    } else {
+      T* o = reinterpret_cast<T*>(out) + row * ldo;
+      const float inv_cols = 1.f / (float)cols;
+      if constexpr (OP == B2_ROW_SOFTMAX) {
+        float m = -INFINITY;
+        for (long long c = threadIdx.x; c < cols; c += TPR) m = nan_max(m, to_f32<T>(xr[c]));
+        m = row_reduce<TPR, RK_MAX>(m, red_v);
+        const float ms = m * kLog2e;
+        float s = 0.f;
+        for (long long c = threadIdx.x; c < cols; c += TPR) s += exp2f(fmaf(to_f32<T>(xr[c]), kLog2e, -ms));
+        s = row_reduce<TPR, RK_SUM>(s, red_v);
+        const float inv = 1.f / s;
+        for (long long c = threadIdx.x; c < cols; c += TPR)
+          o[c] = from_f32<T>(exp2f(fmaf(to_f32<T>(xr[c]), kLog2e, -ms)) * inv);
+      } else if constexpr (OP == B2_ROW_LAYERNORM) {
+        float s = 0.f;
+        for (long long c = threadIdx.x; c < cols; c += TPR) s += to_f32<T>(xr[c]);
+        const float mean = row_reduce<TPR, RK_SUM>(s, red_v) * inv_cols;
+        float q = 0.f;
+        for (long long c = threadIdx.x; c < cols; c += TPR) {
+          const float d = to_f32<T>(xr[c]) - mean;
+          q = fmaf(d, d, q);
+        }
+        const float rstd = rsqrtf(row_reduce<TPR, RK_SUM>(q, red_v) * inv_cols + eps);
+        for (long long c = threadIdx.x; c < cols; c += TPR) {
+          const float g = w ? to_f32<T>(w[c]) : 1.f, bb = bvec ? to_f32<T>(bvec[c]) : 0.f;
+          o[c] = from_f32<T>(fmaf((to_f32<T>(xr[c]) - mean) * rstd, g, bb));
+        }
+      } else if constexpr (OP == B2_ROW_RMSNORM) {
+        float q = 0.f;
+        for (long long c = threadIdx.x; c < cols; c += TPR) {
+          const float t = to_f32<T>(xr[c]);
+          q = fmaf(t, t, q);
+        }
+        const float r = rsqrtf(row_reduce<TPR, RK_SUM>(q, red_v) * inv_cols + eps);
+        for (long long c = threadIdx.x; c < cols; c += TPR) {
+          const float g = w ? to_f32<T>(w[c]) : 1.f;
+          o[c] = from_f32<T>(to_f32<T>(xr[c]) * r * g);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------- split-row reduction
+// Few long rows: grid (splits, rows). Each CTA reduces one chunk into the
+// workspace; a second launch folds the partials in chunk order.
+struct Partial {
+  float v;
+  int pad;
+  long long i;
+};
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(512)
+row_split_partial_kernel(const T* __restrict__ x, long long cols, long long ldx, long long chunk,
+                         Partial* __restrict__ ws) {
+  constexpr int TPR = 512;
+  __shared__ float red_v[32];
+  __shared__ long long red_i[32];
+  const long long row = blockIdx.y;
+  const long long c0 = (long long)blockIdx.x * chunk;
+  const long long c1 = c0 + chunk < cols ? c0 + chunk : cols;
+  const T* xr = x + row * ldx;
+  Partial p;
+  p.pad = 0;
+  const bool vec_ok = (sizeof(T) == 4) && ((reinterpret_cast<uintptr_t>(xr + c0) & 15) == 0);
+  if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+    constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+    float bv = MAXI ? -INFINITY : INFINITY;
+    long long bi = 0x7fffffffffffffffLL;
+    for (long long c = c0 + threadIdx.x; c < c1; c += TPR) {
+      const float t = to_f32<T>(xr[c]);
+      if (arg_better<MAXI>(t, c, bv, bi)) { bv = t; bi = c; }
+    }
+    row_reduce_arg<TPR, MAXI>(bv, bi, red_v, red_i);
+    p.v = bv; p.i = bi;
+  } else {
+    constexpr int KIND = OP == B2_ROW_SUM ? RK_SUM : (OP == B2_ROW_MAX ? RK_MAX : RK_MIN);
+    float a = KIND == RK_SUM ? 0.f : (KIND == RK_MAX ? -INFINITY : INFINITY);
+    long long c = c0;
+    if (vec_ok) {
+      const long long nv = (c1 - c0) / 4;
+      const float4* xv = reinterpret_cast<const float4*>(xr + c0);
+      for (long long k = threadIdx.x; k < nv; k += TPR) {
+        const float4 f = __ldcs(xv + k);
+        if (KIND == RK_SUM) a += (f.x + f.y) + (f.z + f.w);
+        else if (KIND == RK_MAX) a = nan_max(nan_max(a, f.x), nan_max(nan_max(f.y, f.z), f.w));
+        else a = nan_min(nan_min(a, f.x), nan_min(nan_min(f.y, f.z), f.w));
+      }
+      c = c0 + nv * 4;
+    }
+    for (long long cc = c + threadIdx.x; cc < c1; cc += TPR) {
+      const float t = to_f32<T>(xr[cc]);
+      if (KIND == RK_SUM) a += t;
+      else if (KIND == RK_MAX) a = nan_max(a, t);
+      else a = nan_min(a, t);
+    }
+    a = row_reduce<TPR, KIND>(a, red_v);
+    p.v = a; p.i = 0;
+  }
+  if (threadIdx.x == 0) ws[row * gridDim.x + blockIdx.x] = p;
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(32)
+row_split_final_kernel(const Partial* __restrict__ ws, int splits, void* __restrict__ out) {
+  const long long row = blockIdx.x;
+  const Partial* pr = ws + row * splits;
+  const int lane = threadIdx.x;
+  if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+    constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+    float bv = MAXI ? -INFINITY : INFINITY;
+    long long bi = 0x7fffffffffffffffLL;
+    for (int s = lane; s < splits; s += 32)
+      if (arg_better<MAXI>(pr[s].v, pr[s].i, bv, bi)) { bv = pr[s].v; bi = pr[s].i; }
+    group_arg<32, MAXI>(bv, bi);
+    if (lane == 0) reinterpret_cast<long long*>(out)[row] = bi;
+  } else {
+    float a = OP == B2_ROW_SUM ? 0.f : (OP == B2_ROW_MAX ? -INFINITY : INFINITY);
+    for (int s = lane; s < splits; s += 32) {
+      if (OP == B2_ROW_SUM) a += pr[s].v;
+      else if (OP == B2_ROW_MAX) a = nan_max(a, pr[s].v);
+      else a = nan_min(a, pr[s].v);
+    }
+    if (OP == B2_ROW_SUM) a = group_sum<32>(a);
+    else if (OP == B2_ROW_MAX) a = group_max<32>(a);
+    else a = group_min<32>(a);
+    if (lane == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
+  }
+}
+
+// -------------------------------------------------------------- dispatch
+int g_num_sms = 0;
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+template <typename T, int OP, int TPR, int VPT>
+int launch_reg(const void* x, const void* w, const void* b, void* out, long long rows, int cols,
+               long long ldx, long long ldo, float eps, cudaStream_t st) {
+  constexpr int BLOCK = TPR > 32 ? TPR : 256;
+  constexpr int RPB = BLOCK / TPR;
+  long long blocks = (rows + RPB - 1) / RPB;
+  const long long cap = (long long)num_sms() * 64;
+  if (blocks > cap) blocks = cap;
+  row_reg_kernel<T, OP, TPR, VPT><<<(unsigned)blocks, BLOCK, 0, st>>>(
+      (const T*)x, (const T*)w, (const T*)b, out, rows, cols, ldx, ldo, eps);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+// Pick threads-per-row so each thread holds 16 elements (32 for the longest rows).
+template <typename T, int OP>
+int dispatch_reg(const void* x, const void* w, const void* b, void* out, long long rows, int cols,
+                 long long ldx, long long ldo, float eps, cudaStream_t st) {
+  constexpr int EPV = Vec<T>::N;
+  constexpr int V16 = 16 / EPV;  // vectors per thread for 16 elements
+  const int per16 = (cols + 15) / 16;
+  if (per16 <= 8) return launch_reg<T, OP, 8, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 16) return launch_reg<T, OP, 16, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 32) return launch_reg<T, OP, 32, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 64) return launch_reg<T, OP, 64, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 128) return launch_reg<T, OP, 128, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 256) return launch_reg<T, OP, 256, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 512) return launch_reg<T, OP, 512, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  if (per16 <= 1024) return launch_reg<T, OP, 1024, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  return launch_reg<T, OP, 1024, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+}
+
+constexpr long long kSplitChunk = 1 << 16;  // elements per CTA on the split path
+
+bool use_split(int op, long long rows, long long cols) {
+  const bool scalar_op = op == B2_ROW_SUM || op == B2_ROW_MAX || op == B2_ROW_MIN ||
+                         op == B2_ROW_ARGMAX || op == B2_ROW_ARGMIN;
+  return scalar_op && cols >= 4 * kSplitChunk && rows < 2LL * num_sms();
+}
+
+template <typename T, int OP>
+int dispatch_op(const void* x, const void* w, const void* b, void* out, long long rows,
+                long long cols, long long ldx, long long ldo, float eps, void* ws, size_t ws_bytes,
+                cudaStream_t st) {
+  constexpr int EPV = Vec<T>::N;
+  if (use_split(OP, rows, cols)) {
+    const long long splits = (cols + kSplitChunk - 1) / kSplitChunk;
+    const size_t need = (size_t)(rows * splits) * sizeof(Partial);
+    if (ws == nullptr || ws_bytes < need) {
+      set_error("b2_row_op: split-row path needs %zu workspace bytes, got %zu", need, ws_bytes);
+      return B2_EINVAL;
+    }
+    if ((reinterpret_cast<uintptr_t>(ws) & 15) != 0) {
+      set_error("b2_row_op: workspace must be 16-byte aligned");
+      return B2_EINVAL;
+    }
+    dim3 grid((unsigned)splits, (unsigned)rows);
+    row_split_partial_kernel<T, OP><<<grid, 512, 0, st>>>((const T*)x, cols, ldx, kSplitChunk,
+                                                          (Partial*)ws);
+    B2_CHECK_LAUNCH();
+    row_split_final_kernel<T, OP><<<(unsigned)rows, 32, 0, st>>>((const Partial*)ws, (int)splits, out);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+  }
+  const bool row_out = OP == B2_ROW_SOFTMAX || OP == B2_ROW_LAYERNORM || OP == B2_ROW_RMSNORM;
+  auto al16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool aligned = cols % EPV == 0 && ldx % EPV == 0 && al16(x) && al16(w) && al16(b) &&
+                       (!row_out || (ldo % EPV == 0 && al16(out)));
+  if (aligned && cols <= 32 * 1024 * (EPV == 8 ? 2 : 1) && cols > 0) {
+    return dispatch_reg<T, OP>(x, w, b, out, rows, (int)cols, ldx, ldo, eps, st);
+  }
+  long long blocks = rows;
+  const long long cap = (long long)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  row_generic_kernel<T, OP><<<(unsigned)blocks, 512, 0, st>>>((const T*)x, (const T*)w,
+                                                               (const T*)b, out, rows, cols, ldx,
+                                                               ldo, eps);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+template <typename T>
+int dispatch_type(int op, const void* x, const void* w, const void* b, void* out, long long rows,
+                  long long cols, long long ldx, long long ldo, float eps, void* ws,
+                  size_t ws_bytes, cudaStream_t st) {
+  switch (op) {
+#define B2_ROW_CASE(OPV) \
+  case OPV: return dispatch_op<T, OPV>(x, w, b, out, rows, cols, ldx, ldo, eps, ws, ws_bytes, st);
+    B2_ROW_CASE(B2_ROW_SOFTMAX)
+    B2_ROW_CASE(B2_ROW_LAYERNORM)
+    B2_ROW_CASE(B2_ROW_RMSNORM)
+    B2_ROW_CASE(B2_ROW_SUM)
+    B2_ROW_CASE(B2_ROW_MAX)
+    B2_ROW_CASE(B2_ROW_ARGMAX)
+    B2_ROW_CASE(B2_ROW_MIN)
+    B2_ROW_CASE(B2_ROW_ARGMIN)
+#undef B2_ROW_CASE
+    default:
+      set_error("b2_row_op: unknown op %d", op);
+      return B2_EINVAL;
+  }
+}
+
+}  // namespace
+
+size_t row_op_workspace(int op, long long rows, long long cols) {
+  if (rows <= 0 || cols <= 0 || !use_split(op, rows, cols)) return 0;
+  const long long splits = (cols + kSplitChunk - 1) / kSplitChunk;
+  return (size_t)(rows * splits) * sizeof(Partial);
+}
+
+int row_op_launch(int op, const void* x, const void* w, const void* b, void* out, long long rows,
+                  long long cols, long long ldx, long long ldo, float eps, int dtype, void* ws,
+                  size_t ws_bytes, cudaStream_t st) {
+  switch (dtype) {
+    case B2_F32: return dispatch_type<float>(op, x, w, b, out, rows, cols, ldx, ldo, eps, ws, ws_bytes, st);
+    case B2_F16: return dispatch_type<__half>(op, x, w, b, out, rows, cols, ldx, ldo, eps, ws, ws_bytes, st);
+    case B2_BF16: return dispatch_type<__nv_bfloat16>(op, x, w, b, out, rows, cols, ldx, ldo, eps, ws, ws_bytes, st);
+    default:
+      set_error("b2_row_op: unsupported dtype %d", dtype);
+      return B2_EINVAL;
+  }
+}
+
+uint32_t row_read_status(bool clear) {
+  uint32_t s = 0;
+  cudaMemcpyFromSymbol(&s, g_row_status, sizeof(s));
+  if (clear) {
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(g_row_status, &z, sizeof(z));
+  }
+  return s;
+}
+
+}  // namespace b2
