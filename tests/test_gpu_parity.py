@@ -21,6 +21,10 @@ from triton_msl_b200 import workloads as W
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 F32_ABS, LOWP_REL = O.TOL_F32_ABS, O.TOL_LOWP_REL
+# A bf16 result rounded from the exact value is already up to 2^-8 (half an
+# ulp) away from it, relative to its own magnitude, so bf16 outputs get that
+# storage allowance on top of the 2e-3 arithmetic bound.
+BF16_STORE = 2.0 ** -8
 
 
 def _rand(shape, dtype, seed, std=1.0):
@@ -29,12 +33,13 @@ def _rand(shape, dtype, seed, std=1.0):
 
 
 def _check(got, ref, dtype):
-    if dtype == torch.float32:
+    if dtype == torch.float32 and got.dtype == torch.float32:
         err = O.max_abs_err(got, ref)
         assert err <= F32_ABS, f"max-abs {err:.3e} > {F32_ABS}"
     else:
+        tol = LOWP_REL + (BF16_STORE if got.dtype == torch.bfloat16 else 0.0)
         err = O.normwise_err(got, ref)
-        assert err <= LOWP_REL, f"normwise {err:.3e} > {LOWP_REL}"
+        assert err <= tol, f"normwise {err:.3e} > {tol:.3e}"
 
 
 # ------------------------------------------------------------------ attention

@@ -179,7 +179,7 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out, in
     return B2_EINVAL;
   }
   if (rows == 0 || (cols == 0 && row_out)) return B2_OK;
-  if (!x || !out) {
+  if (!out || (cols > 0 && !x)) {
     set_error("b2_row_op: null pointer argument");
     return B2_EINVAL;
   }

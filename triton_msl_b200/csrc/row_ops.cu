@@ -15,7 +15,7 @@
 // B200 design: HBM-bound, so each row is read exactly once with 16-byte
 // streaming loads into registers (up to 32 elements per thread), reduced with
 // warp shuffles (+ one shared-memory hop across warps), and written once with
-// 16-byte streaming stores. Rows up to 32768 fp32 (65536 fp16) stay register
+// 16-byte streaming stores. Rows up to 32768 elements stay register
 // resident. Longer or unaligned rows take a strided path that re-reads the row
 // (second read mostly hits L2). Few-but-long rows for the scalar reductions are
 // split across CTAs, with partials in caller-provided workspace.
@@ -575,7 +575,7 @@ int dispatch_op(const void* x, const void* w, const void* b, void* out, long lon
   auto al16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const bool aligned = cols % EPV == 0 && ldx % EPV == 0 && al16(x) && al16(w) && al16(b) &&
                        (!row_out || (ldo % EPV == 0 && al16(out)));
-  if (aligned && cols <= 32 * 1024 * (EPV == 8 ? 2 : 1) && cols > 0) {
+  if (aligned && cols <= 32 * 1024 && cols > 0) {
     return dispatch_reg<T, OP>(x, w, b, out, rows, (int)cols, ldx, ldo, eps, st);
   }
   long long blocks = rows;
