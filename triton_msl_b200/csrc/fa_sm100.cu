@@ -69,6 +69,64 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// ---- packed fp32x2 arithmetic (one issue slot for two lanes' worth of work)
+typedef unsigned long long f2_t;
+__device__ __forceinline__ f2_t f2_pack(float a, float b) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(f2_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_add_rm(f2_t a, f2_t b) {
+  f2_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for two lanes on the FMA pipe, x clamped to [-126, 126].
+// Range reduction: t = x + 1.5*2^23 rounded toward -inf holds floor(x) in the
+// low mantissa bits of t; f = x - floor(x) lies in [0, 1); 2^f comes from a
+// cubic p(f) = 1 + f*(c1 + f*(c2 + f*c3)) whose coefficients are this file's
+// own weighted least-squares fit of 2^f on [0, 1] with p(0) = 1 and p(1) = 2
+// (max relative error 1.03e-4, below the fp16 / bf16 rounding of P); floor(x)
+// is then added into the exponent field.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c1 = 0.6954244f, c2 = 0.22630768f, c3 = 0.07826797f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const f2_t x = f2_pack(x0, x1);
+  const f2_t t = f2_add_rm(x, f2_pack(kMagic, kMagic));
+  const f2_t xi = f2_add(t, f2_pack(-kMagic, -kMagic));
+  const f2_t f = f2_fma(xi, f2_pack(-1.f, -1.f), x);
+  f2_t p = f2_fma(f, f2_pack(c3, c3), f2_pack(c2, c2));
+  p = f2_fma(f, p, f2_pack(c1, c1));
+  p = f2_fma(f, p, f2_pack(1.f, 1.f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  // bits(t) << 23 == floor(x) << 23 (mod 2^32): the magic's own bits shift out.
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -253,30 +311,36 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     for (int j = 0; j < n_t; ++j) {
       if (!mbar_wait(&bars->s_full[t], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) { ok = false; break; }
       tc_fence_after();
+      // All four 32-column loads in flight, then one wait; the empty asm
+      // statements pin every use of the loaded registers after the wait.
+      uint32_t sr[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c)
+        tmem_ld32(tS[t] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) asm volatile("" : "+r"(sr[i]));
       float s[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS[t] + lane_off + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-      }
+      for (int i = 0; i < kBN; ++i) s[i] = __uint_as_float(sr[i]);
       const int kbase = j * kBN;
       const bool need_mask = (kbase + kBN > S) || (causal && kbase + kBN - 1 > m0 + t * kBM);
-      float mx = -INFINITY;
       if (need_mask) {
+        const int lim = min(S - kbase, causal ? qrow - kbase + 1 : kBN);  // keys [0, lim) kept
 #pragma unroll
-        for (int i = 0; i < kBN; ++i) {
-          const int key = kbase + i;
-          if (key >= S || (causal && key > qrow)) s[i] = -INFINITY;
-          mx = fmaxf(mx, s[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kBN; ++i) mx = fmaxf(mx, s[i]);
+        for (int i = 0; i < kBN; ++i)
+          if (i >= lim) s[i] = -INFINITY;
       }
-      mx *= scale_log2;
+      // Row max: four independent 3-input max chains.
+      float mq[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int i = 4; i < kBN; i += 8) {
+        mq[0] = fmax3(mq[0], s[i], s[i + 1]);
+        mq[1] = fmax3(mq[1], s[i + 2], s[i + 3]);
+        mq[2] = fmax3(mq[2], s[i + 4], i + 5 < kBN ? s[i + 5] : -INFINITY);
+        mq[3] = fmax3(mq[3], i + 6 < kBN ? s[i + 6] : -INFINITY, i + 7 < kBN ? s[i + 7] : -INFINITY);
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale_log2;
       // Rescale only when some row of this warp grew its max by > 2^8.
       const bool grow = mx > m_run + kRescaleThreshold;
       const bool warp_rescale = __any_sync(0xffffffffu, grow);
@@ -287,14 +351,33 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         m_run = m_new;
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      float rowsum = 0.f;
+      // p = 2^(s*scale_log2 - m). The MUFU ex2 costs 8 cycles per warp
+      // instruction per SM sub-partition (measured on B200); with two tiles per
+      // sub-partition that alone would equal the tensor core's time per key
+      // block, so 3 of every 8 key pairs use exp2_poly2 on the FMA pipe.
+      const f2_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_use, -m_use);
+      f2_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t p[kBN / 2];
 #pragma unroll
       for (int i = 0; i < kBN / 2; ++i) {
-        const float p0 = ex2(fmaf(s[2 * i], scale_log2, -m_use));
-        const float p1 = ex2(fmaf(s[2 * i + 1], scale_log2, -m_use));
-        rowsum += p0 + p1;
+        const f2_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
+        float x0, x1, p0, p1;
+        f2_unpack(x2, x0, x1);
+        if ((i & 7) < 5) {
+          p0 = ex2(x0);
+          p1 = ex2(x1);
+        } else {
+          exp2_poly2(x0, x1, p0, p1);
+        }
+        acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(p0, p1));
         p[i] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+      }
+      float rowsum;
+      {
+        const f2_t a01 = f2_add(acc2[0], acc2[1]), a23 = f2_add(acc2[2], acc2[3]);
+        float u0, u1;
+        f2_unpack(f2_add(a01, a23), u0, u1);
+        rowsum = u0 + u1;
       }
       l_run = l_run * alpha + rowsum;
 #pragma unroll
