@@ -15,7 +15,7 @@ import threading
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libb2msl.so"
+LIB_PATH = Path(os.environ.get("B2MSL_LIBRARY", PKG / "libb2msl.so"))
 
 B2_OK, B2_EINVAL, B2_EUNSUPPORTED, B2_ELAUNCH, B2_ETIMEOUT = 0, -1, -2, -3, -4
 B2_F32, B2_F16, B2_BF16, B2_I64 = 0, 1, 2, 3

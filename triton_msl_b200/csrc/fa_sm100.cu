@@ -232,25 +232,34 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const uint32_t q0 = smem_addr(sQ), k0 = smem_addr(sK), v0 = smem_addr(sV);
       bool ok = true;
       bool issued = false;
+      // Base descriptors per buffer, computed once: each MMA issue below is a
+      // 64-bit add of a compile-time offset plus the tcgen05.mma itself.
+      const uint64_t dq0 = sdesc(q0, 16, Cfg::kSBO, Cfg::kSwz);
+      const uint64_t dq1 = sdesc(q0 + Cfg::kTileBytes, 16, Cfg::kSBO, Cfg::kSwz);
+      const uint64_t dk0 = sdesc(k0, 16, Cfg::kSBO, Cfg::kSwz);
+      const uint64_t dk1 = sdesc(k0 + Cfg::kTileBytes, 16, Cfg::kSBO, Cfg::kSwz);
+      const uint64_t dv0 = sdesc(v0, Cfg::kAtomTileBytes, Cfg::kSBO, Cfg::kSwz);
+      const uint64_t dv1 = sdesc(v0 + Cfg::kTileBytes, Cfg::kAtomTileBytes, Cfg::kSBO, Cfg::kSwz);
       auto qk = [&](int t, int ks) {
-        const uint32_t qa = q0 + t * Cfg::kTileBytes, ka = k0 + ks * Cfg::kTileBytes;
+        const uint64_t da = t ? dq1 : dq0, db = ks ? dk1 : dk0;
+        const uint32_t d = t ? tS[1] : tS[0];
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k * 16 / Cfg::kAtom) * Cfg::kAtomTileBytes + (k * 16 % Cfg::kAtom) * 2;
-          mma_f16_ss(tS[t], sdesc(qa + off, 16, Cfg::kSBO, Cfg::kSwz),
-                     sdesc(ka + off, 16, Cfg::kSBO, Cfg::kSwz), idS, k > 0 ? 1u : 0u);
+          const uint32_t off16 =
+              ((k * 16 / Cfg::kAtom) * Cfg::kAtomTileBytes + (k * 16 % Cfg::kAtom) * 2) >> 4;
+          mma_f16_ss(d, da + off16, db + off16, idS, k > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int t, int vs, bool accumulate) {
-        const uint32_t va = v0 + vs * Cfg::kTileBytes;
+        const uint64_t db = vs ? dv1 : dv0;
+        const uint32_t d = t ? tO[1] : tO[0], pa = t ? tS[1] : tS[0];
+        const uint32_t acc0 = accumulate ? 1u : 0u;
 #pragma unroll
         for (int k = 0; k < kBN / 16; ++k) {
           // A = P_t: 16 keys = 8 packed TMEM columns per step.
           // B = V: MN-major, 16 key rows = 16 * atom-row bytes per step,
-          //        64-wide D chunks kAtomTileBytes apart.
-          mma_f16_ts(tO[t], tS[t] + k * 8,
-                     sdesc(va + k * 16 * Cfg::kAtomBytes, Cfg::kAtomTileBytes, Cfg::kSBO, Cfg::kSwz),
-                     idO, (accumulate || k > 0) ? 1u : 0u);
+          //        64-wide D chunks kAtomTileBytes apart (the LBO).
+          mma_f16_ts(d, pa + k * 8, db + ((k * 16 * Cfg::kAtomBytes) >> 4), idO, k > 0 ? 1u : acc0);
         }
       };
       do {
