@@ -137,6 +137,31 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out,
               float eps, int dtype, void* workspace, size_t ws_bytes,
               void* stream);
 
+/*
+ * Row sum / max / min / argmax / argmin over x[rows, cols] (row stride ld_x,
+ * unit column stride) that allocates nothing and takes no workspace.
+ *
+ * No counterpart in the reference: it is an addition for callers that cannot
+ * allocate device memory when they reduce -- code inside a custom allocator or
+ * an out-of-memory handler, or a host runtime that forbids cudaMalloc after
+ * start-up. It always runs the split-row kernels: results are identical to
+ * b2_row_op's wherever b2_row_op takes its split-row path (few long rows) and
+ * differ only by fp32 summation order elsewhere; indices are exact.
+ *  - Scratch is a fixed 256 KiB array in the library's device image, held on
+ *    every GPU that loads the library until the process exits. It holds
+ *    rows * ceil(cols / 65536) <= 16384 partial results; larger requests fail
+ *    with B2_EINVAL (use b2_row_op with a workspace for those).
+ *  - The first call on a device looks up the array's device address with that
+ *    device current; make that first call before any stream capture.
+ *  - All calls share the one array: calls whose kernels overlap on the GPU
+ *    (different streams, or different host threads, same device) race.
+ *    Every scratch slot a call reads is written by the same call first, so
+ *    nothing needs clearing between calls.
+ * out: int64 indices for argmax/argmin, else x's dtype. cols must be > 0.
+ */
+int b2_row_reduce_noalloc(int op, const void* x, void* out, int64_t rows, int64_t cols,
+                          int64_t ld_x, int dtype, void* stream);
+
 /* Scratch bytes a call with these arguments needs (0 = none).
  * kind: 0 = b2_gemm (a0=M, a1=N, a2=K, a3=in_dtype),
  *       1 = b2_row_op (a0=op, a1=rows, a2=cols, a3=dtype),

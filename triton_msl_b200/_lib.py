@@ -37,6 +37,8 @@ SIGNATURES = {
     "b2_row_op": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4
                   + [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                      ctypes.c_void_p]),
+    "b2_row_reduce_noalloc": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+                              + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p]),
     "b2_query_workspace": (ctypes.c_size_t, [ctypes.c_int] + [ctypes.c_int64] * 4),
     "b2_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_uint32)]),

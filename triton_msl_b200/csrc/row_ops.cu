@@ -22,6 +22,7 @@
 #include "b2_common.cuh"
 
 #include <cfloat>
+#include <mutex>
 
 namespace b2 {
 namespace {
@@ -642,3 +643,112 @@ uint32_t row_read_status(bool clear) {
 }
 
 }  // namespace b2
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the split-row reduction.
+//
+// Some callers cannot allocate device memory at the point where they reduce:
+// code running inside a custom allocator or an out-of-memory handler, a
+// library that must not touch the process's CUDA memory pool, or a host
+// runtime that forbids cudaMalloc after start-up. For them the split path's
+// scratch lives in a fixed array in this library's device image instead of a
+// caller-provided workspace. Every GPU that loads the library reserves it
+// until the process exits.
+namespace b2 {
+namespace {
+
+constexpr long long kNoAllocMaxPartials = 16384;  // 16384 x 16 B = 256 KiB per device
+static __device__ __align__(256) Partial g_row_noalloc_scratch[kNoAllocMaxPartials];
+
+// Device address of the array, looked up once per device with that device
+// current (host code only sees a host-side stand-in under the array's name).
+constexpr int kNoAllocMaxDev = 64;
+Partial* g_noalloc_ptr[kNoAllocMaxDev];
+cudaError_t g_noalloc_err[kNoAllocMaxDev];
+std::once_flag g_noalloc_once[kNoAllocMaxDev];
+
+template <typename T, int OP>
+int noalloc_launch(const void* x, void* out, long long rows, long long cols, long long ldx,
+                   Partial* scratch, long long splits, cudaStream_t st) {
+  dim3 grid((unsigned)splits, (unsigned)rows);
+  row_split_partial_kernel<T, OP><<<grid, 512, 0, st>>>((const T*)x, cols, ldx, kSplitChunk, scratch);
+  B2_CHECK_LAUNCH();
+  row_split_final_kernel<T, OP><<<(unsigned)rows, 32, 0, st>>>(scratch, (int)splits, out);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+template <typename T>
+int noalloc_dispatch(int op, const void* x, void* out, long long rows, long long cols,
+                     long long ldx, Partial* scratch, long long splits, cudaStream_t st) {
+  switch (op) {
+    case B2_ROW_SUM: return noalloc_launch<T, B2_ROW_SUM>(x, out, rows, cols, ldx, scratch, splits, st);
+    case B2_ROW_MAX: return noalloc_launch<T, B2_ROW_MAX>(x, out, rows, cols, ldx, scratch, splits, st);
+    case B2_ROW_MIN: return noalloc_launch<T, B2_ROW_MIN>(x, out, rows, cols, ldx, scratch, splits, st);
+    case B2_ROW_ARGMAX: return noalloc_launch<T, B2_ROW_ARGMAX>(x, out, rows, cols, ldx, scratch, splits, st);
+    case B2_ROW_ARGMIN: return noalloc_launch<T, B2_ROW_ARGMIN>(x, out, rows, cols, ldx, scratch, splits, st);
+  }
+  set_error("b2_row_reduce_noalloc: op %d is not a scalar reduction (sum/max/min/argmax/argmin)", op);
+  return B2_EINVAL;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" __attribute__((visibility("default")))
+int b2_row_reduce_noalloc(int op, const void* x, void* out, int64_t rows, int64_t cols,
+                          int64_t ld_x, int dtype, void* stream) {
+  using namespace b2;
+  clear_error();
+  if (op != B2_ROW_SUM && op != B2_ROW_MAX && op != B2_ROW_MIN && op != B2_ROW_ARGMAX &&
+      op != B2_ROW_ARGMIN) {
+    set_error("b2_row_reduce_noalloc: op %d is not a scalar reduction (sum/max/min/argmax/argmin)", op);
+    return B2_EINVAL;
+  }
+  if (dtype != B2_F32 && dtype != B2_F16 && dtype != B2_BF16) {
+    set_error("b2_row_reduce_noalloc: unsupported dtype %d", dtype);
+    return B2_EINVAL;
+  }
+  if (rows < 0 || cols <= 0 || ld_x < cols) {
+    set_error("b2_row_reduce_noalloc: invalid shape rows=%lld cols=%lld ld_x=%lld (cols must be > 0)",
+              (long long)rows, (long long)cols, (long long)ld_x);
+    return B2_EINVAL;
+  }
+  if (rows == 0) return B2_OK;
+  if (!x || !out) {
+    set_error("b2_row_reduce_noalloc: null pointer argument");
+    return B2_EINVAL;
+  }
+  const long long splits = (cols + kSplitChunk - 1) / kSplitChunk;
+  if (rows > kNoAllocMaxPartials || rows * splits > kNoAllocMaxPartials) {
+    set_error("b2_row_reduce_noalloc: rows * ceil(cols / %lld) = %lld exceeds the fixed scratch of "
+              "%lld partials; use b2_row_op with a workspace instead",
+              kSplitChunk, rows * splits, kNoAllocMaxPartials);
+    return B2_EINVAL;
+  }
+  int dev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDev) {
+    set_error("b2_row_reduce_noalloc: device ordinal %d out of range", dev);
+    return B2_EINVAL;
+  }
+  // First call on this device: resolve the array's device address (the
+  // current device is the one being set up).
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_row_noalloc_scratch);
+    g_noalloc_ptr[dev] = static_cast<Partial*>(p);
+  });
+  if (g_noalloc_err[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr) {
+    set_error("b2_row_reduce_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+              cudaGetErrorString(g_noalloc_err[dev]));
+    return B2_ELAUNCH;
+  }
+  Partial* scratch = g_noalloc_ptr[dev];
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case B2_F32: return noalloc_dispatch<float>(op, x, out, rows, cols, ld_x, scratch, splits, st);
+    case B2_F16: return noalloc_dispatch<__half>(op, x, out, rows, cols, ld_x, scratch, splits, st);
+    default: return noalloc_dispatch<__nv_bfloat16>(op, x, out, rows, cols, ld_x, scratch, splits, st);
+  }
+}
