@@ -11,4 +11,8 @@ from .ops import (  # noqa: F401
     row_min, row_argmax, row_argmin,
 )
 
+from . import compile_backend as _cb
+
+_cb.register()  # torch.compile(..., backend="b2msl")
+
 __version__ = "0.1.0"

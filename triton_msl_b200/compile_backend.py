@@ -1,0 +1,315 @@
+"""``torch.compile`` backend that routes the hot-path patterns to the b2msl ops.
+
+The reference reaches its templates from ``torch.compile`` by registering a
+Triton scheduling for MPS (``register_metal_triton_backend``,
+triton_msl/inductor/__init__.py:52-153) and letting its pattern detectors
+(attention ``generic_lowerer.py:679-835``, matmul epilogue
+``_lowerer_detection.py:1150-1364``, softmax / LayerNorm
+``_lowerer_detection.py:1828-2074``) pick templates from the generated
+kernels. Here the same patterns are recognised directly in the FX graph that
+Dynamo captures and replaced by calls to the custom ops:
+
+* ``F.scaled_dot_product_attention(q, k, v[, is_causal, scale])`` and the
+  explicit ``softmax(q @ k.transpose(-2, -1) * s) @ v`` chain -> ``flash_attn_fwd``
+* ``F.linear(x, w[, b])`` / ``torch.matmul`` / ``@`` / ``torch.addmm`` on 2-D
+  operands, with a following ``relu`` / ``gelu`` / ``silu`` folded in -> ``gemm``
+* ``softmax(x, dim=-1)``, ``F.layer_norm`` over the last dim, ``F.rms_norm``
+  over the last dim, ``sum / amax / amin / argmax / argmin(dim=-1)`` -> row ops
+
+A node is rewritten only when its traced example value says the replacement
+is exact: CUDA tensors, float32/float16/bfloat16, shapes the ops accept. The
+rest of the graph runs as captured (``inner="eager"``) or through Inductor
+(``inner="inductor"``).
+"""
+from __future__ import annotations
+
+import operator
+from typing import Callable, List, Optional
+
+import torch
+import torch.fx as fx
+import torch.nn.functional as F
+
+from . import ops as b2ops
+
+_FLOATS = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def _val(n):
+    if isinstance(n, fx.Node):
+        return n.meta.get("example_value", n.meta.get("val"))
+    return None
+
+
+def _ok_tensor(n, allow_cpu: bool, ndim: Optional[int] = None) -> bool:
+    v = _val(n)
+    if not isinstance(v, torch.Tensor):
+        return False
+    if v.dtype not in _FLOATS:
+        return False
+    if not allow_cpu and v.device.type != "cuda":
+        return False
+    if ndim is not None and v.dim() != ndim:
+        return False
+    return True
+
+
+def _arg(node: fx.Node, i: int, name: str, default=None):
+    if len(node.args) > i:
+        return node.args[i]
+    return node.kwargs.get(name, default)
+
+
+def _is_last_dim(dim, v) -> bool:
+    if isinstance(dim, (list, tuple)):
+        if len(dim) != 1:
+            return False
+        dim = dim[0]
+    return isinstance(dim, int) and v is not None and dim in (-1, v.dim() - 1)
+
+
+_SOFTMAX = {torch.softmax, F.softmax, torch.nn.functional.softmax, "softmax"}
+_MATMUL = {torch.matmul, operator.matmul, torch.mm, "matmul", "mm"}
+_ACTS = {torch.relu: "relu", F.relu: "relu", "relu": "relu", F.gelu: "gelu",
+         F.silu: "silu", torch.nn.functional.silu: "silu"}
+_LINEAR = {F.linear, torch._C._nn.linear}
+_LAYERNORM = {F.layer_norm, torch.layer_norm}
+_RMSNORM = {f for f in (getattr(F, "rms_norm", None), getattr(torch, "rms_norm", None)) if f is not None}
+_ROWRED = {torch.sum: "sum", "sum": "sum", torch.amax: "max", "amax": "max",
+           torch.amin: "min", "amin": "min", torch.argmax: "argmax", "argmax": "argmax",
+           torch.argmin: "argmin", "argmin": "argmin"}
+
+
+def _target_key(node: fx.Node):
+    if node.op == "call_method":
+        return node.target
+    if node.op == "call_function":
+        return node.target
+    return None
+
+
+def _in(node, table) -> bool:
+    k = _target_key(node)
+    try:
+        return k in table
+    except TypeError:
+        return False
+
+
+# ------------------------------------------------------------ replacements
+def _linear_act(x, w, b, act):
+    """x[..., K] @ w[N, K]^T (+ b) with activation, through the GEMM op."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    y = b2ops.gemm(x2, w.t(), b, act)
+    return y.reshape(*lead, w.shape[0])
+
+
+def _matmul_act(a, b, act):
+    return b2ops.gemm(a, b, None, act)
+
+
+def _addmm_act(bias, a, b, act):
+    return b2ops.gemm(a, b, bias, act)
+
+
+def _sdpa(q, k, v, causal, scale):
+    return b2ops.flash_attn_fwd(q, k, v, causal=causal, sm_scale=scale)
+
+
+def _rowred(x, kind):
+    return getattr(b2ops, f"row_{kind}")(x)
+
+
+def _layer_norm(x, w, b, eps):
+    return b2ops.row_layernorm(x, w, b, eps)
+
+
+def _rms_norm(x, w, eps):
+    return b2ops.row_rmsnorm(x, w, eps)
+
+
+class Rewriter:
+    """Pattern-rewrites one FX graph in place; counts what it replaced."""
+
+    def __init__(self, gm: fx.GraphModule, allow_cpu: bool = False):
+        self.gm = gm
+        self.g = gm.graph
+        self.allow_cpu = allow_cpu
+        self.replaced: List[str] = []
+
+    def _replace(self, node: fx.Node, fn: Callable, args, tag: str, last: Optional[fx.Node] = None):
+        anchor = last or node
+        with self.g.inserting_after(anchor):
+            new = self.g.call_function(fn, tuple(args))
+        new.meta.update(anchor.meta)
+        anchor.replace_all_uses_with(new)
+        self.replaced.append(tag)
+        return new
+
+    def _single_user_act(self, node: fx.Node):
+        users = list(node.users)
+        if len(users) != 1:
+            return None, None
+        u = users[0]
+        if u.op in ("call_function", "call_method") and _in(u, _ACTS) and len(u.args) == 1 and not u.kwargs:
+            return u, _ACTS[_target_key(u)]
+        if u.op == "call_function" and u.target is F.gelu and u.kwargs.get("approximate", "none") == "tanh":
+            return u, "gelu_tanh"
+        return None, None
+
+    def run(self) -> List[str]:
+        # Consumers first, so a chain (softmax inside explicit attention, an
+        # activation after a matmul) is seen whole before its parts.
+        for node in reversed(list(self.g.nodes)):
+            if node.op not in ("call_function", "call_method") or not node.users:
+                continue
+            try:
+                self._visit(node)
+            except Exception:  # a pattern that does not fit leaves the node alone
+                continue
+        self.g.eliminate_dead_code()
+        self.gm.recompile()
+        return self.replaced
+
+    def _visit(self, node: fx.Node):
+        t = _target_key(node)
+        ac = self.allow_cpu
+        # ---- attention
+        if t is F.scaled_dot_product_attention:
+            q, k, v = node.args[:3]
+            mask = _arg(node, 3, "attn_mask")
+            drop = _arg(node, 4, "dropout_p", 0.0)
+            causal = _arg(node, 5, "is_causal", False)
+            scale = node.kwargs.get("scale")
+            if mask is None and drop == 0.0 and all(_ok_tensor(x, ac, 4) for x in (q, k, v)):
+                qv, kv, vv = (_val(x) for x in (q, k, v))
+                if qv.shape == kv.shape == vv.shape and qv.dtype == kv.dtype == vv.dtype \
+                        and qv.shape[-1] <= 128:
+                    s = scale if scale is not None else qv.shape[-1] ** -0.5
+                    self._replace(node, _sdpa, (q, k, v, bool(causal), float(s)), "attention")
+            return
+        # ---- explicit attention chain: matmul(softmax(matmul(q, k^T) * s), v)
+        if _in(node, _MATMUL) and len(node.args) == 2:
+            p, v = node.args
+            if isinstance(p, fx.Node) and _in(p, _SOFTMAX) and len(p.users) == 1:
+                hit = self._explicit_attention(node, p, v)
+                if hit:
+                    return
+            a, b = node.args
+            if _ok_tensor(a, ac, 2) and _ok_tensor(b, ac, 2) and _val(a).dtype == _val(b).dtype:
+                act_node, act = self._single_user_act(node)
+                self._replace(node, _matmul_act, (a, b, act or "none"),
+                              "matmul" + (f"+{act}" if act else ""), act_node)
+            return
+        # ---- linear (+ activation)
+        if _in(node, _LINEAR):
+            x, w = node.args[:2]
+            b = _arg(node, 2, "bias")
+            if _ok_tensor(x, ac) and _ok_tensor(w, ac, 2) and _val(x).dtype == _val(w).dtype \
+                    and (b is None or _ok_tensor(b, ac, 1)):
+                act_node, act = self._single_user_act(node)
+                self._replace(node, _linear_act, (x, w, b, act or "none"),
+                              "linear" + (f"+{act}" if act else ""), act_node)
+            return
+        if t is torch.addmm and len(node.args) == 3 and not node.kwargs:
+            bias, a, b = node.args
+            if _ok_tensor(bias, ac, 1) and _ok_tensor(a, ac, 2) and _ok_tensor(b, ac, 2):
+                act_node, act = self._single_user_act(node)
+                self._replace(node, _addmm_act, (bias, a, b, act or "none"),
+                              "addmm" + (f"+{act}" if act else ""), act_node)
+            return
+        # ---- row family
+        if _in(node, _SOFTMAX):
+            x = node.args[0] if node.op == "call_function" else node.args[0]
+            dim = _arg(node, 1, "dim")
+            if _ok_tensor(x, ac) and _is_last_dim(dim, _val(x)) and node.kwargs.get("dtype") is None:
+                self._replace(node, b2ops.row_softmax, (x,), "softmax")
+            return
+        if _in(node, _LAYERNORM):
+            x, shape = node.args[:2]
+            w = _arg(node, 2, "weight")
+            b = _arg(node, 3, "bias")
+            eps = _arg(node, 4, "eps", 1e-5)
+            xv = _val(x)
+            if _ok_tensor(x, ac) and tuple(shape) == (xv.shape[-1],) \
+                    and all(p is None or (_ok_tensor(p, ac, 1) and _val(p).dtype == xv.dtype) for p in (w, b)):
+                self._replace(node, _layer_norm, (x, w, b, float(eps)), "layer_norm")
+            return
+        if _in(node, _RMSNORM):
+            x, shape = node.args[:2]
+            w = _arg(node, 2, "weight")
+            eps = _arg(node, 3, "eps")
+            xv = _val(x)
+            if eps is not None and _ok_tensor(x, ac) and tuple(shape) == (xv.shape[-1],) \
+                    and (w is None or (_ok_tensor(w, ac, 1) and _val(w).dtype == xv.dtype)):
+                self._replace(node, _rms_norm, (x, w, float(eps)), "rms_norm")
+            return
+        if _in(node, _ROWRED):
+            kind = _ROWRED[t]
+            x = node.args[0]
+            dim = _arg(node, 1, "dim")
+            keep = _arg(node, 2, "keepdim", False)
+            xv = _val(x)
+            if _ok_tensor(x, ac) and _is_last_dim(dim, xv) and not keep and node.kwargs.get("dtype") is None \
+                    and xv.dim() >= 1 and xv.shape[-1] > 0:
+                self._replace(node, _rowred, (x, kind), f"row_{kind}")
+            return
+
+    def _explicit_attention(self, out_mm: fx.Node, sm: fx.Node, v) -> bool:
+        if not _is_last_dim(_arg(sm, 1, "dim"), _val(sm)):
+            return False
+        s = sm.args[0]
+        scale = 1.0
+        if isinstance(s, fx.Node) and _target_key(s) in (operator.mul, torch.mul, "mul", operator.truediv, torch.div, "div") \
+                and len(s.users) == 1:
+            x, c = s.args
+            if isinstance(c, fx.Node) or not isinstance(c, (int, float)):
+                return False
+            scale = float(c) if _target_key(s) in (operator.mul, torch.mul, "mul") else 1.0 / float(c)
+            s = x
+        if not (isinstance(s, fx.Node) and _in(s, _MATMUL) and len(s.users) == 1):
+            return False
+        q, kt = s.args
+        if not (isinstance(kt, fx.Node) and _target_key(kt) in (torch.transpose, "transpose")):
+            return False
+        k = kt.args[0]
+        dims = tuple(d % 4 for d in kt.args[1:3]) if len(kt.args) >= 3 else ()
+        if sorted(dims) != [2, 3]:
+            return False
+        if not all(_ok_tensor(x, self.allow_cpu, 4) for x in (q, k, v)):
+            return False
+        qv, kv, vv = _val(q), _val(k), _val(v)
+        if not (qv.shape == kv.shape == vv.shape and qv.dtype == kv.dtype == vv.dtype and qv.shape[-1] <= 128):
+            return False
+        self._replace(out_mm, _sdpa, (q, k, v, False, scale), "attention(explicit)")
+        return True
+
+
+def rewrite(gm: fx.GraphModule, allow_cpu: bool = False) -> List[str]:
+    """Rewrite ``gm`` in place; returns the tags of the replaced patterns."""
+    return Rewriter(gm, allow_cpu).run()
+
+
+last_rewrites: List[str] = []
+
+
+def b2msl_backend(gm: fx.GraphModule, example_inputs, inner: str = "eager"):
+    """Dynamo backend: rewrite the hot-path patterns, then run eagerly or via Inductor."""
+    global last_rewrites
+    last_rewrites = rewrite(gm)
+    if inner == "inductor":
+        from torch._inductor.compile_fx import compile_fx
+        return compile_fx(gm, example_inputs)
+    return gm.forward
+
+
+def register() -> None:
+    """Register ``backend="b2msl"`` (and ``"b2msl_inductor"``) with torch.compile."""
+    from torch._dynamo import register_backend
+    from torch._dynamo.backends.registry import _BACKENDS
+    if "b2msl" not in _BACKENDS:
+        register_backend(name="b2msl")(b2msl_backend)
+    if "b2msl_inductor" not in _BACKENDS:
+        register_backend(name="b2msl_inductor")(
+            lambda gm, ex: b2msl_backend(gm, ex, inner="inductor"))
