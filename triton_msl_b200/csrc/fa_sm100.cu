@@ -226,7 +226,10 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
-    if (lane == 0) {
+    // The whole warp runs the issue loop (so loop-invariant operands stay
+    // warp-uniform) and one elected lane issues each tcgen05 instruction.
+    {
+      const bool leader = elect_one();
       constexpr uint32_t idS = idesc_f16(kBM, kBN, BF16, false, false);  // Q K^T: both K-major
       constexpr uint32_t idO = idesc_f16(kBM, D, BF16, false, true);     // P V: V is MN-major
       const uint32_t q0 = smem_addr(sQ), k0 = smem_addr(sK), v0 = smem_addr(sV);
@@ -247,7 +250,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off16 =
               ((k * 16 / Cfg::kAtom) * Cfg::kAtomTileBytes + (k * 16 % Cfg::kAtom) * 2) >> 4;
-          mma_f16_ss(d, da + off16, db + off16, idS, k > 0 ? 1u : 0u);
+          if (leader) mma_f16_ss(d, da + off16, db + off16, idS, k > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int t, int vs, bool accumulate) {
@@ -259,17 +262,17 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           // A = P_t: 16 keys = 8 packed TMEM columns per step.
           // B = V: MN-major, 16 key rows = 16 * atom-row bytes per step,
           //        64-wide D chunks kAtomTileBytes apart (the LBO).
-          mma_f16_ts(d, pa + k * 8, db + ((k * 16 * Cfg::kAtomBytes) >> 4), idO, k > 0 ? 1u : acc0);
+          if (leader) mma_f16_ts(d, pa + k * 8, db + ((k * 16 * Cfg::kAtomBytes) >> 4), idO, k > 0 ? 1u : acc0);
         }
       };
       do {
         if (!mbar_wait(&bars->q_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
         if (!mbar_wait(&bars->k_full[0], 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
         tc_fence_after();
-        if (n0 > 0) { qk(0, 0); mma_commit(&bars->s_full[0]); }
+        if (n0 > 0) { qk(0, 0); if (leader) mma_commit(&bars->s_full[0]); }
         qk(1, 0);
-        mma_commit(&bars->s_full[1]);
-        mma_commit(&bars->k_empty[0]);
+        if (leader) mma_commit(&bars->s_full[1]);
+        if (leader) mma_commit(&bars->k_empty[0]);
         issued = true;
         for (int j = 0; j < n; ++j) {
           const int vs = j & 1;
@@ -284,22 +287,22 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (j + 1 < n) {
             if (!mbar_wait(&bars->k_full[ks], ((j + 1) >> 1) & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
             tc_fence_after();
-            if (j + 1 < n0) { qk(0, ks); mma_commit(&bars->s_full[0]); }
+            if (j + 1 < n0) { qk(0, ks); if (leader) mma_commit(&bars->s_full[0]); }
           }
           if (!mbar_wait(&bars->p_full[1], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
           tc_fence_after();
           pv(1, vs, j > 0);
-          mma_commit(&bars->v_empty[vs]);
+          if (leader) mma_commit(&bars->v_empty[vs]);
           if (j + 1 < n) {
             qk(1, ks);
-            mma_commit(&bars->s_full[1]);
-            mma_commit(&bars->k_empty[ks]);
+            if (leader) mma_commit(&bars->s_full[1]);
+            if (leader) mma_commit(&bars->k_empty[ks]);
           }
         }
-        if (ok) mma_commit(&bars->o_full);
+        if (ok) if (leader) mma_commit(&bars->o_full);
       } while (false);
       if (issued) {
-        mma_commit(&bars->done);
+        if (leader) mma_commit(&bars->done);
         const unsigned long long t0 = globaltimer();
         while (!mbar_test(smem_addr(&bars->done), 0)) {
           if (globaltimer() - t0 > kWaitLimitNs) { atomicOr(&g_fa_status, DEV_TIMEOUT_MMA); break; }
@@ -372,7 +375,15 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const f2_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
         float x0, x1, p0, p1;
         f2_unpack(x2, x0, x1);
+#if defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 4
+        if (!((i & 7) == 2 || (i & 7) == 5 || (i & 7) == 7)) {
+#elif defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 5
+        if ((i & 3) != 3) {
+#elif defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 6
+        if ((i & 7) != 7) {
+#else
         if ((i & 7) < 5) {
+#endif
           p0 = ex2(x0);
           p1 = ex2(x1);
         } else {
