@@ -21,6 +21,8 @@
 //  * Epilogue: tcgen05.ld 32 columns at a time, alpha, + bias[n], activation,
 //    convert, 16-byte stores.
 //  * Every mbarrier wait is bounded (see sm100.cuh).
+#include <cstring>
+
 #include "sm100.cuh"
 
 namespace b2 {
@@ -37,6 +39,10 @@ constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr int kGroupM = 16;                    // raster: 16 M-tiles per group
 constexpr uint32_t kTmemCols = 512;
+// Epilogue staging: per epilogue warp two 32x32 output blocks (<= 4 KB each),
+// written swizzled and sent to global memory with TMA tensor stores.
+constexpr uint32_t kStageOutBytes = 4096;
+constexpr uint32_t kEpiSmem = 4 * 2 * kStageOutBytes;
 
 struct __align__(8) GemmBarriers {
   uint64_t full[kStages];
@@ -54,6 +60,41 @@ __device__ __forceinline__ float bias_at(const void* b, int dt, int n) {
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(b)[n]);
 }
 
+// 32 bias values for columns [n0, n0+32): vector loads (same address in every
+// lane, served as a broadcast) when aligned and in range, else guarded scalars.
+__device__ __forceinline__ void load_bias32(const void* bias, int dt, int n0, int N, float (&bv)[32]) {
+  if (bias == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = 0.f;
+    return;
+  }
+  const bool full = n0 + 32 <= N && (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+  if (full && dt == B2_F32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bias) + n0);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const float4 q = __ldg(p + v);
+      bv[4 * v] = q.x; bv[4 * v + 1] = q.y; bv[4 * v + 2] = q.z; bv[4 * v + 3] = q.w;
+    }
+  } else if (full) {
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(bias) + n0);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint4 q = __ldg(p + v);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&q);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint16_t b16 = h[e];
+        bv[8 * v + e] = dt == B2_F16 ? __half2float(__ushort_as_half(b16))
+                                     : __bfloat162float(__ushort_as_bfloat16(b16));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = n0 + j < N ? bias_at(bias, dt, n0 + j) : 0.f;
+  }
+}
+
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = kGroupM * num_n;
   const int g = t / per_group;
@@ -67,13 +108,15 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 template <typename TO, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmC, int use_tma_store,
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
                   int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + kStages * kStageBytes);
+  uint8_t* sOut = smem + kStages * kStageBytes;
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + kStages * kStageBytes + kEpiSmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
@@ -154,7 +197,9 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue
-    if (lane == 0) {
+    // Whole warp runs the loop (warp-uniform operands); one elected lane issues.
+    {
+      const bool leader = elect_one();
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -181,17 +226,17 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const uint64_t ad = sdesc(a0 + k * 32, 16, 1024, kSwizzle128);
             const uint64_t bd = B_MN ? sdesc(b0 + k * 16 * 128, 64 * kBK * 2, 1024, kSwizzle128)
                                      : sdesc(b0 + k * 32, 16, 1024, kSwizzle128);
-            mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (leader) mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           issued = true;
-          mma_commit(&bars->empty[stage]);
+          if (leader) mma_commit(&bars->empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&bars->acc_full[acc]);
+        if (leader) mma_commit(&bars->acc_full[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -199,7 +244,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
       // Drain: all MMAs issued by this thread have retired before TMEM is freed.
       if (issued) {
-        mma_commit(&bars->done);
+        if (leader) mma_commit(&bars->done);
         const unsigned long long t0 = globaltimer();
         while (!mbar_test(smem_addr(&bars->done), 0)) {
           if (globaltimer() - t0 > kWaitLimitNs) {
@@ -228,14 +273,42 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         tmem_ld32(tbase + c * 32, r);
         tmem_ld_wait();
         const int n0 = nb * kBN + c * 32;
-        if (row >= M || n0 >= N) continue;
+        if (n0 >= N) continue;  // warp-uniform
+        float bv[32];
+        load_bias32(bias, bias_dt, n0, N, bv);
         float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(r[j]) * alpha;
-          if (bias != nullptr && n0 + j < N) x += bias_at(bias, bias_dt, n0 + j);
-          f[j] = apply_act(x, act);
+        for (int j = 0; j < 32; ++j) f[j] = apply_act(fmaf(__uint_as_float(r[j]), alpha, bv[j]), act);
+        if (use_tma_store) {
+          // Row `lane` of a 32x32 block -> swizzled staging -> one TMA store
+          // per warp (rows >= M and columns >= N are clipped by the TMA unit).
+          constexpr int RB = 32 * (int)sizeof(TO);  // staging row bytes: 64 or 128
+          uint8_t* stg = sOut + ((warp - 2) * 2 + (c & 1)) * kStageOutBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          const int swz = ((lane * RB) >> 7) & (RB / 16 - 1);
+#pragma unroll
+          for (int ch = 0; ch < RB / 16; ++ch) {
+            uint4 u;
+            if constexpr (sizeof(TO) == 2) {
+              TO* h = reinterpret_cast<TO*>(&u);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) h[e] = from_f32<TO>(f[ch * 8 + e]);
+            } else {
+              u = make_uint4(__float_as_uint(f[ch * 4]), __float_as_uint(f[ch * 4 + 1]),
+                             __float_as_uint(f[ch * 4 + 2]), __float_as_uint(f[ch * 4 + 3]));
+            }
+            *reinterpret_cast<uint4*>(stg + lane * RB + ((ch ^ swz) * 16)) = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(stg, &tmC, n0, mb * kBM + quarter * 32);
+            bulk_commit_group();
+          }
+          continue;
         }
+        if (row >= M) continue;
         if (vec_ok && n0 + 32 <= N) {
           if constexpr (sizeof(TO) == 2) {
             uint4* dst = reinterpret_cast<uint4*>(crow + n0);
@@ -267,6 +340,8 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         acc_phase ^= 1u;
       }
     }
+    // Output stores still in flight must finish before the CTA exits.
+    if (use_tma_store && lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -280,11 +355,12 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 int g_sms = 0;
 
 template <typename TO, bool B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const void* bias, int bias_dt, void* C,
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
+           const void* bias, int bias_dt, void* C,
            long long M, long long N, long long K, long long ldc, float alpha, int act,
            uint32_t idesc, int vec_ok, cudaStream_t st) {
   auto kern = gemm_sm100_kernel<TO, B_MN>;
-  const size_t smem = 1024 + kStages * kStageBytes + sizeof(GemmBarriers);
+  const size_t smem = 1024 + kStages * kStageBytes + kEpiSmem + sizeof(GemmBarriers);
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   if (g_sms == 0) {
     int dev;
@@ -293,7 +369,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const void* bias, int b
   }
   const long long tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = (int)(tiles < g_sms ? tiles : g_sms);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, tc, use_tma, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
                                       alpha, act, idesc, vec_ok);
   B2_CHECK_LAUNCH();
   return B2_OK;
@@ -349,16 +425,31 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
     return B2_EUNSUPPORTED;
   }
   if (bias == nullptr) bias_dt = B2_F32;
+  // Output through TMA tensor stores when C's base and row pitch allow it.
+  CUtensorMap tc;
+  int use_tma = 0;
+  if (vec_ok && s[4] >= N) {
+    const CUtensorMapDataType cdt = out_dt == B2_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : out_dt == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)s[4] * osz};
+    const uint32_t box[2] = {32, 32};
+    use_tma = encode_tmap(&tc, cdt, 2, C, dims, strides, box,
+                          osz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
+    clear_error();
+  }
+  if (!use_tma) memset(&tc, 0, sizeof(tc));
   switch (out_dt) {
     case B2_F16:
-      return b_mn ? launch<__half, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<__half, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<__half, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<__half, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
     case B2_BF16:
-      return b_mn ? launch<__nv_bfloat16, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<__nv_bfloat16, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<__nv_bfloat16, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<__nv_bfloat16, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
     case B2_F32:
-      return b_mn ? launch<float, true>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<float, false>(ta, tb, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<float, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
+                  : launch<float, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;
