@@ -39,10 +39,15 @@ constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr int kGroupM = 16;                    // raster: 16 M-tiles per group
 constexpr uint32_t kTmemCols = 512;
-// Epilogue staging: per epilogue warp two 32x32 output blocks (<= 4 KB each),
-// written swizzled and sent to global memory with TMA tensor stores.
-constexpr uint32_t kStageOutBytes = 4096;
-constexpr uint32_t kEpiSmem = 4 * 2 * kStageOutBytes;
+// Epilogue staging: per epilogue warp two 32x32 output blocks, written
+// swizzled and sent to global memory with TMA tensor stores, plus two bias
+// tiles. With fp32 output the blocks are twice as large, so that variant uses
+// a 3-stage operand ring to stay inside 227 KB of shared memory.
+template <typename TO> struct EpiCfg {
+  static constexpr int kRing = sizeof(TO) == 4 ? 3 : 4;
+  static constexpr uint32_t kOutBytes = 32 * 32 * sizeof(TO);
+  static constexpr uint32_t kEpiSmem = 4 * 2 * kOutBytes + 2 * kBN * 4;
+};
 
 struct __align__(8) GemmBarriers {
   uint64_t full[kStages];
@@ -58,41 +63,6 @@ __device__ __forceinline__ float bias_at(const void* b, int dt, int n) {
   if (dt == B2_F32) return __ldg(reinterpret_cast<const float*>(b) + n);
   if (dt == B2_F16) return __half2float(reinterpret_cast<const __half*>(b)[n]);
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(b)[n]);
-}
-
-// 32 bias values for columns [n0, n0+32): vector loads (same address in every
-// lane, served as a broadcast) when aligned and in range, else guarded scalars.
-__device__ __forceinline__ void load_bias32(const void* bias, int dt, int n0, int N, float (&bv)[32]) {
-  if (bias == nullptr) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) bv[j] = 0.f;
-    return;
-  }
-  const bool full = n0 + 32 <= N && (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
-  if (full && dt == B2_F32) {
-    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bias) + n0);
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const float4 q = __ldg(p + v);
-      bv[4 * v] = q.x; bv[4 * v + 1] = q.y; bv[4 * v + 2] = q.z; bv[4 * v + 3] = q.w;
-    }
-  } else if (full) {
-    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(bias) + n0);
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const uint4 q = __ldg(p + v);
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(&q);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint16_t b16 = h[e];
-        bv[8 * v + e] = dt == B2_F16 ? __half2float(__ushort_as_half(b16))
-                                     : __bfloat162float(__ushort_as_bfloat16(b16));
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) bv[j] = n0 + j < N ? bias_at(bias, dt, n0 + j) : 0.f;
-  }
 }
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -111,12 +81,16 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                   const __grid_constant__ CUtensorMap tmC, int use_tma_store,
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
                   int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok) {
+  constexpr int kRing = EpiCfg<TO>::kRing;
+  constexpr uint32_t kStageOutBytes = EpiCfg<TO>::kOutBytes;
+  constexpr uint32_t kEpiSmem = EpiCfg<TO>::kEpiSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + kStages * kABytes;
-  uint8_t* sOut = smem + kStages * kStageBytes;
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + kStages * kStageBytes + kEpiSmem);
+  uint8_t* sB = smem + kRing * kABytes;
+  uint8_t* sOut = smem + kRing * kStageBytes;
+  float* sBias = reinterpret_cast<float*>(sOut + 4 * 2 * kStageOutBytes);  // [2][kBN]
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(smem + kRing * kStageBytes + kEpiSmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
@@ -125,7 +99,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
@@ -174,7 +148,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], kb * kBK, nb * kBN);
           }
           filled |= 1u << stage;
-          if (++stage == kStages) {
+          if (++stage == kRing) {
             stage = 0;
             phase ^= 1u;
           }
@@ -182,7 +156,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
       // Never leave with bulk copies in flight into this CTA's shared memory:
       // wait (bounded) for the latest fill of every stage to land.
-      for (int s = 0; s < kStages; ++s) {
+      for (int s = 0; s < kRing; ++s) {
         if (!(filled & (1u << s))) continue;
         // the latest fill of stage s used parity (phase of that round)
         const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
@@ -230,7 +204,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           }
           issued = true;
           if (leader) mma_commit(&bars->empty[stage]);
-          if (++stage == kStages) {
+          if (++stage == kRing) {
             stage = 0;
             phase ^= 1u;
           }
@@ -259,9 +233,22 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     int acc = 0;
     uint32_t acc_phase = 0;
+    int tile_iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
+      // This tile's bias columns into shared memory (double-buffered by tile
+      // parity), loaded while the accumulator is still being computed.
+      float* tb_bias = sBias + (tile_iter & 1) * kBN;
+      if (bias != nullptr) {
+        const int et = threadIdx.x - 64;  // 0..127 over the four epilogue warps
+        for (int cidx = et; cidx < kBN; cidx += 128) {
+          const int n = nb * kBN + cidx;
+          tb_bias[cidx] = n < N ? bias_at(bias, bias_dt, n) : 0.f;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      ++tile_iter;
       if (!mbar_wait(&bars->acc_full[acc], acc_phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_MMA)) break;
       tc_fence_after();
       const int row = mb * kBM + quarter * 32 + lane;
@@ -275,7 +262,16 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const int n0 = nb * kBN + c * 32;
         if (n0 >= N) continue;  // warp-uniform
         float bv[32];
-        load_bias32(bias, bias_dt, n0, N, bv);
+        if (bias != nullptr) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const float4 q = *reinterpret_cast<const float4*>(tb_bias + c * 32 + 4 * v);
+            bv[4 * v] = q.x; bv[4 * v + 1] = q.y; bv[4 * v + 2] = q.z; bv[4 * v + 3] = q.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) bv[j] = 0.f;
+        }
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = apply_act(fmaf(__uint_as_float(r[j]), alpha, bv[j]), act);
@@ -360,7 +356,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
            long long M, long long N, long long K, long long ldc, float alpha, int act,
            uint32_t idesc, int vec_ok, cudaStream_t st) {
   auto kern = gemm_sm100_kernel<TO, B_MN>;
-  const size_t smem = 1024 + kStages * kStageBytes + kEpiSmem + sizeof(GemmBarriers);
+  const size_t smem = 1024 + EpiCfg<TO>::kRing * kStageBytes + EpiCfg<TO>::kEpiSmem + sizeof(GemmBarriers);
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   if (g_sms == 0) {
     int dev;
