@@ -130,8 +130,8 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int H, int S,
-                int num_qblk, long long soz, long long soh, long long som, float scale_log2,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                int H, int S, int num_qblk, float scale_log2,
                 int causal) {
   using Cfg = FaCfg<D>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -426,29 +426,42 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (ok && mbar_wait(&bars->o_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* orow = reinterpret_cast<T*>(out) + (long long)b * soz + (long long)h * soh + (long long)qrow * som;
+      // O rows -> swizzled staging in the (now idle) K/V ring -> TMA stores of
+      // one 32-row block per warp; rows >= S are clipped by the TMA unit.
+      uint8_t* stg = sK + (warp - 4) * (32 * D * 2);
+      const int swz = ((lane * Cfg::kAtomBytes) >> 7) & (Cfg::kAtomBytes / 16 - 1);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tO[t] + lane_off + c * 32, r);
         tmem_ld_wait();
-        if (qrow < S) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+        // 32 columns = 64 bytes = 4 chunks of 16 B, inside atom a = (c*32)/kAtom
+        const int col0 = c * 32;
+        uint8_t* atom = stg + (col0 / Cfg::kAtom) * (32 * Cfg::kAtomBytes);
+        const int chunk0 = (col0 % Cfg::kAtom) * 2 / 16;
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 u;
-            u.x = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 0]) * inv, __uint_as_float(r[v * 8 + 1]) * inv)
-                       : pack_half2(__uint_as_float(r[v * 8 + 0]) * inv, __uint_as_float(r[v * 8 + 1]) * inv);
-            u.y = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv)
-                       : pack_half2(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv);
-            u.z = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv)
-                       : pack_half2(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv);
-            u.w = BF16 ? pack_bf162(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv)
-                       : pack_half2(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv);
-            dst[v] = u;
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float f0 = __uint_as_float(r[v * 8 + 2 * e]) * inv;
+            const float f1 = __uint_as_float(r[v * 8 + 2 * e + 1]) * inv;
+            w[e] = BF16 ? pack_bf162(f0, f1) : pack_half2(f0, f1);
           }
+          *reinterpret_cast<uint4*>(atom + lane * Cfg::kAtomBytes + (((chunk0 + v) ^ swz) * 16)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        for (int at = 0; at < Cfg::kNumAtoms; ++at)
+          tma_store_4d(stg + at * (32 * Cfg::kAtomBytes), &tmO, at * Cfg::kAtom,
+                       m0 + t * kBM + quarter * 32, h, b);
+        bulk_commit_group();
+        bulk_wait_group<0>();
+      }
+      __syncwarp();
     }
   }
 
@@ -475,6 +488,13 @@ int launch(const void* q, const void* k, const void* v, void* o, long long B, lo
     const uint32_t box[4] = {(uint32_t)Cfg::kAtom, 128, 1, 1};
     if (!encode_tmap(&tm[i], tdt, 4, ptrs[i], dims, strides, box, swz)) return B2_ELAUNCH;
   }
+  CUtensorMap tmo;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)s[14] * 2, (uint64_t)s[13] * 2, (uint64_t)s[12] * 2};
+    const uint32_t box[4] = {(uint32_t)Cfg::kAtom, 32, 1, 1};
+    if (!encode_tmap(&tmo, tdt, 4, o, dims, strides, box, swz)) return B2_ELAUNCH;
+  }
   auto kern = fa_sm100_kernel<D, BF16>;
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem));
   const int num_qblk = (int)((S + 2 * kBM - 1) / (2 * kBM));
@@ -483,8 +503,8 @@ int launch(const void* q, const void* k, const void* v, void* o, long long B, lo
     set_error("b2_fa_fwd: grid too large");
     return B2_EINVAL;
   }
-  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, st>>>(tm[0], tm[1], tm[2], o, (int)H, (int)S, num_qblk,
-                                                      s[12], s[13], s[14], sm_scale * kLog2e, causal);
+  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, st>>>(tm[0], tm[1], tm[2], tmo, (int)H, (int)S, num_qblk,
+                                                      sm_scale * kLog2e, causal);
   B2_CHECK_LAUNCH();
   return B2_OK;
 }

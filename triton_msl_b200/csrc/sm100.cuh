@@ -124,6 +124,14 @@ __device__ __forceinline__ void tma_store_2d(const void* src, const void* map, i
       "r"(smem_addr(src)), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_4d(const void* src, const void* map, int x, int y, int z,
+                                             int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          map),
+      "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
