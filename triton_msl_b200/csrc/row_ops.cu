@@ -40,8 +40,8 @@ __device__ __forceinline__ float nan_min(float a, float b) {
 }
 // true if (a, ia) beats (b, ib) for argmax (MAXI) / argmin (!MAXI): NaN is the
 // extreme value, ties and NaN-vs-NaN go to the lower index (torch semantics).
-template <bool MAXI>
-__device__ __forceinline__ bool arg_better(float a, long long ia, float b, long long ib) {
+template <bool MAXI, typename I>
+__device__ __forceinline__ bool arg_better(float a, I ia, float b, I ib) {
   const bool an = a != a, bn = b != b;
   if (an || bn) return an && (!bn || ia < ib);
   if (MAXI) return a > b || (a == b && ia < ib);
@@ -68,12 +68,12 @@ __device__ __forceinline__ float group_min(float v) {
   for (int o = G / 2; o > 0; o >>= 1) v = nan_min(v, __shfl_xor_sync(0xffffffffu, v, o, G));
   return v;
 }
-template <int G, bool MAXI>
-__device__ __forceinline__ void group_arg(float& v, long long& i) {
+template <int G, bool MAXI, typename I>
+__device__ __forceinline__ void group_arg(float& v, I& i) {
 #pragma unroll
   for (int o = G / 2; o > 0; o >>= 1) {
     float ov = __shfl_xor_sync(0xffffffffu, v, o, G);
-    long long oi = __shfl_xor_sync(0xffffffffu, i, o, G);
+    I oi = __shfl_xor_sync(0xffffffffu, i, o, G);
     if (arg_better<MAXI>(ov, oi, v, i)) { v = ov; i = oi; }
   }
 }
@@ -105,8 +105,8 @@ __device__ __forceinline__ float row_reduce(float v, float* red_smem) {
   return v;
 }
 
-template <int TPR, bool MAXI>
-__device__ __forceinline__ void row_reduce_arg(float& v, long long& i, float* red_v, long long* red_i) {
+template <int TPR, bool MAXI, typename I>
+__device__ __forceinline__ void row_reduce_arg(float& v, I& i, float* red_v, I* red_i) {
   group_arg<(TPR < 32 ? TPR : 32), MAXI>(v, i);
   if constexpr (TPR > 32) {
     constexpr int NW = TPR / 32;
@@ -114,7 +114,7 @@ __device__ __forceinline__ void row_reduce_arg(float& v, long long& i, float* re
     if (lane == 0) { red_v[wid] = v; red_i[wid] = i; }
     __syncthreads();
     float tv = lane < NW ? red_v[lane] : red_v[0];
-    long long ti = lane < NW ? red_i[lane] : red_i[0];
+    I ti = lane < NW ? red_i[lane] : red_i[0];
     group_arg<32, MAXI>(tv, ti);
     v = tv; i = ti;
   }
@@ -179,7 +179,7 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
   constexpr int RPB = BLOCK / TPR;  // rows per block
   static_assert(TPR <= 32 || RPB == 1, "multi-row blocks need TPR <= 32");
   __shared__ float red_v[32];
-  __shared__ long long red_i[32];
+  __shared__ int red_i[32];
 
   const int sub = threadIdx.x % TPR;          // thread index inside the row
   const int rloc = threadIdx.x / TPR;         // row slot inside the block
@@ -214,20 +214,26 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
       if (row_ok && sub == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
     } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
       constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+      // This thread visits its columns in increasing order, so a strict
+      // comparison keeps the earliest of equal values and the first NaN;
+      // 32-bit indices (rows are < 2^31 columns) until the int64 store.
       float bv = MAXI ? -INFINITY : INFINITY;
-      long long bi = 0x7fffffffffffffffLL;
+      int bi = 0x7fffffff;
 #pragma unroll
       for (int i = 0; i < VPT; ++i)
         if (ok[i]) {
 #pragma unroll
           for (int j = 0; j < EPV; ++j) {
-            const long long ci = (long long)(sub + i * TPR) * EPV + j;
-            if (arg_better<MAXI>(v[i][j], ci, bv, bi)) { bv = v[i][j]; bi = ci; }
+            const float x = v[i][j];
+            const int ci = (sub + i * TPR) * EPV + j;
+            const bool take = (MAXI ? x > bv : x < bv) || (x != x && bv == bv) || bi == 0x7fffffff;
+            bv = take ? x : bv;
+            bi = take ? ci : bi;
           }
         }
       if constexpr (TPR > 32) __syncthreads();
       row_reduce_arg<TPR, MAXI>(bv, bi, red_v, red_i);
-      if (row_ok && sub == 0) reinterpret_cast<long long*>(out)[row] = bi;
+      if (row_ok && sub == 0) reinterpret_cast<long long*>(out)[row] = (long long)bi;
       if constexpr (TPR > 32) __syncthreads();
     } else if constexpr (OP == B2_ROW_SOFTMAX) {
       float m = -INFINITY;
