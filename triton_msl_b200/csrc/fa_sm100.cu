@@ -45,7 +45,8 @@ struct __align__(8) FaBarriers {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_full;
+  uint64_t o_full, o_empty;
+  uint64_t q_empty;
   uint64_t done;
   uint32_t tmem_base;
   int abort_flag;
@@ -60,7 +61,9 @@ struct FaCfg {
   static constexpr uint32_t kTileBytes = 128 * D * 2;       // one 128-row tile
   static constexpr uint32_t kAtomTileBytes = 128 * kAtomBytes;
   static constexpr uint32_t kSBO = 8 * kAtomBytes;          // 8-row group pitch
-  static constexpr size_t kSmem = 1024 + 6 * kTileBytes + sizeof(FaBarriers);
+  // output staging: per softmax warp one 32-row x atom-wide block
+  static constexpr uint32_t kOutStageBytes = 32 * kAtomBytes;
+  static constexpr size_t kSmem = 1024 + 6 * kTileBytes + 8 * kOutStageBytes + sizeof(FaBarriers);
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -131,7 +134,7 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                int H, int S, int num_qblk, float scale_log2,
+                int H, int BH, int S, int num_qblk, float scale_log2,
                 int causal) {
   using Cfg = FaCfg<D>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -140,26 +143,40 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   uint8_t* sQ = smem;                              // 2 tiles
   uint8_t* sK = smem + 2 * Cfg::kTileBytes;        // 2 stages
   uint8_t* sV = smem + 4 * Cfg::kTileBytes;        // 2 stages
-  FaBarriers* bars = reinterpret_cast<FaBarriers*>(smem + 6 * Cfg::kTileBytes);
+  uint8_t* sO = smem + 6 * Cfg::kTileBytes;        // output staging, 8 warps
+  FaBarriers* bars = reinterpret_cast<FaBarriers*>(sO + 8 * Cfg::kOutStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BH = gridDim.x / num_qblk;
-  // Heaviest query blocks first (causal work grows with the block index).
-  const int qblk = num_qblk - 1 - (int)(blockIdx.x / BH);
-  const int bh = blockIdx.x % BH;
-  const int b = bh / H, h = bh % H;
-  const int m0 = qblk * 2 * kBM;
+  const int num_units = num_qblk * BH;
   const int nkv_all = (S + kBN - 1) / kBN;
-  int n1 = nkv_all, n0 = nkv_all;  // key blocks for Q1 / Q0
-  if (causal) {
-    n1 = min((m0 + 2 * kBM + kBN - 1) / kBN, nkv_all);
-    n0 = min((m0 + kBM + kBN - 1) / kBN, nkv_all);
-  }
-  const int n = n1;  // K/V blocks streamed
+  // Unit u -> (query block, batch*head); heaviest query blocks first (causal
+  // work grows with the block index). CTA i takes, in round r, unit
+  // r*G + i (even r) or r*G + G-1-i (odd r): the serpentine order pairs heavy
+  // and light units, matching a longest-first dynamic schedule without any
+  // global counter.
+  auto unit_at = [&](uint32_t r) -> int {
+    const long long base = (long long)r * gridDim.x;
+    const long long u = base + ((r & 1) ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x);
+    return u > 0x7fffffffLL ? 0x7fffffff : (int)u;
+  };
+  auto decode = [&](int u, int& b, int& h, int& m0, int& n0, int& n1) {
+    const int qblk = num_qblk - 1 - u / BH;
+    const int bh = u % BH;
+    b = bh / H;
+    h = bh % H;
+    m0 = qblk * 2 * kBM;
+    n1 = nkv_all;
+    n0 = nkv_all;
+    if (causal) {
+      n1 = min((m0 + 2 * kBM + kBN - 1) / kBN, nkv_all);
+      n0 = min((m0 + kBM + kBN - 1) / kBN, nkv_all);
+    }
+  };
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
@@ -169,12 +186,14 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(&bars->p_full[i], 4);
     }
     mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->o_empty, 8);
     mbar_init(&bars->done, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -191,38 +210,48 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
       bool ok = true;
-      uint32_t k_filled = 0, v_filled = 0;
-      mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int a = 0; a < Cfg::kNumAtoms; ++a)
-          tma_load_4d(sQ + t * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmQ, &bars->q_full,
-                      a * Cfg::kAtom, m0 + t * kBM, h, b);
-      for (int j = 0; j < n && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1u;
-        if (!mbar_wait(&bars->k_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bars->k_full[s], Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kNumAtoms; ++a)
-          tma_load_4d(sK + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmK, &bars->k_full[s],
-                      a * Cfg::kAtom, j * kBN, h, b);
-        k_filled = j + 1;
-        if (!mbar_wait(&bars->v_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bars->v_full[s], Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kNumAtoms; ++a)
-          tma_load_4d(sV + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmV, &bars->v_full[s],
-                      a * Cfg::kAtom, j * kBN, h, b);
-        v_filled = j + 1;
+      uint32_t g = 0;   // K/V blocks issued by this CTA (ring position)
+      uint32_t ui = 0;  // units started
+      for (;; ++ui) {
+        const int u = unit_at(ui);
+        if (u >= num_units || !ok) break;
+        int b, h, m0, n0, n1;
+        decode(u, b, h, m0, n0, n1);
+        // Q of the previous unit is free once its last Q.K^T has been issued.
+        if (!mbar_wait(&bars->q_empty, (ui & 1) ^ 1u, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::kTileBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int a = 0; a < Cfg::kNumAtoms; ++a)
+            tma_load_4d(sQ + t * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmQ, &bars->q_full,
+                        a * Cfg::kAtom, m0 + t * kBM, h, b);
+        for (int j = 0; j < n1; ++j, ++g) {
+          const int s = g & 1;
+          const uint32_t par = ((g >> 1) & 1) ^ 1u;
+          if (!mbar_wait(&bars->k_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->k_full[s], Cfg::kTileBytes);
+          for (int a = 0; a < Cfg::kNumAtoms; ++a)
+            tma_load_4d(sK + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmK, &bars->k_full[s],
+                        a * Cfg::kAtom, j * kBN, h, b);
+          if (!mbar_wait(&bars->v_empty[s], par, abort_flag, &g_fa_status, DEV_TIMEOUT_SLOT)) { ok = false; ++g; break; }
+          mbar_arrive_expect_tx(&bars->v_full[s], Cfg::kTileBytes);
+          for (int a = 0; a < Cfg::kNumAtoms; ++a)
+            tma_load_4d(sV + s * Cfg::kTileBytes + a * Cfg::kAtomTileBytes, &tmV, &bars->v_full[s],
+                        a * Cfg::kAtom, j * kBN, h, b);
+        }
       }
-      // Bounded drain of copies still in flight into this CTA's shared memory.
+      // Bounded drain of copies still in flight into this CTA's shared memory:
+      // the latest fill of each ring slot and of Q.
       const unsigned long long t0 = globaltimer();
       auto drain = [&](uint64_t* bar, uint32_t par) {
         while (!mbar_test(smem_addr(bar), par)) {
           if (globaltimer() - t0 > kWaitLimitNs) { atomicOr(&g_fa_status, DEV_TIMEOUT_TMA); return; }
         }
       };
-      drain(&bars->q_full, 0);
-      for (uint32_t j = (k_filled > 2 ? k_filled - 2 : 0); j < k_filled; ++j) drain(&bars->k_full[j & 1], (j >> 1) & 1);
-      for (uint32_t j = (v_filled > 2 ? v_filled - 2 : 0); j < v_filled; ++j) drain(&bars->v_full[j & 1], (j >> 1) & 1);
+      if (ui > 0) drain(&bars->q_full, (ui - 1) & 1);
+      for (uint32_t j = (g > 2 ? g - 2 : 0); j < g; ++j) {
+        drain(&bars->k_full[j & 1], (j >> 1) & 1);
+        drain(&bars->v_full[j & 1], (j >> 1) & 1);
+      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -265,42 +294,64 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (leader) mma_f16_ts(d, pa + k * 8, db + ((k * 16 * Cfg::kAtomBytes) >> 4), idO, k > 0 ? 1u : acc0);
         }
       };
-      do {
-        if (!mbar_wait(&bars->q_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
-        if (!mbar_wait(&bars->k_full[0], 0, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+      uint32_t g = 0;             // K/V ring position
+      uint32_t gs0 = 0, gs1 = 0;  // P blocks consumed per tile (p_full parity)
+      uint32_t ui = 0;
+      for (;; ++ui) {
+        const int u = unit_at(ui);
+        if (u >= num_units || !ok) break;
+        int b, h, m0, n0, n1;
+        decode(u, b, h, m0, n0, n1);
+        const int n = n1;
+        (void)b; (void)h; (void)m0;
+        if (!mbar_wait(&bars->q_full, ui & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+        if (!mbar_wait(&bars->k_full[g & 1], (g >> 1) & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
         tc_fence_after();
-        if (n0 > 0) { qk(0, 0); if (leader) mma_commit(&bars->s_full[0]); }
-        qk(1, 0);
+        // S of this unit's first block; S_t's TMEM held the previous unit's last
+        // P_t, whose P.V was issued earlier (tcgen05.mma executes in order).
+        if (n0 > 0) { qk(0, g & 1); if (leader) mma_commit(&bars->s_full[0]); }
+        qk(1, g & 1);
         if (leader) mma_commit(&bars->s_full[1]);
-        if (leader) mma_commit(&bars->k_empty[0]);
+        if (leader) mma_commit(&bars->k_empty[g & 1]);
+        if (n == 1 && leader) mma_commit(&bars->q_empty);
         issued = true;
+        // O_0 / O_1 still hold the previous unit's result until the softmax
+        // warps have read it.
+        if (!mbar_wait(&bars->o_empty, (ui & 1) ^ 1u, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
         for (int j = 0; j < n; ++j) {
-          const int vs = j & 1;
-          const uint32_t vph = (j >> 1) & 1;
+          const uint32_t gj = g + j;
+          const int vs = gj & 1;
+          const uint32_t vph = (gj >> 1) & 1;
           if (!mbar_wait(&bars->v_full[vs], vph, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
           if (j < n0) {
-            if (!mbar_wait(&bars->p_full[0], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
+            if (!mbar_wait(&bars->p_full[0], gs0 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
             tc_fence_after();
             pv(0, vs, j > 0);
+            ++gs0;
           }
-          const int ks = (j + 1) & 1;
+          const uint32_t gk = gj + 1;
+          const int ks = gk & 1;
           if (j + 1 < n) {
-            if (!mbar_wait(&bars->k_full[ks], ((j + 1) >> 1) & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
+            if (!mbar_wait(&bars->k_full[ks], (gk >> 1) & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
             tc_fence_after();
             if (j + 1 < n0) { qk(0, ks); if (leader) mma_commit(&bars->s_full[0]); }
           }
-          if (!mbar_wait(&bars->p_full[1], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
+          if (!mbar_wait(&bars->p_full[1], gs1 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
           tc_fence_after();
           pv(1, vs, j > 0);
+          ++gs1;
           if (leader) mma_commit(&bars->v_empty[vs]);
           if (j + 1 < n) {
             qk(1, ks);
             if (leader) mma_commit(&bars->s_full[1]);
             if (leader) mma_commit(&bars->k_empty[ks]);
+            if (j + 2 == n && leader) mma_commit(&bars->q_empty);  // last Q.K^T of the unit
           }
         }
-        if (ok) if (leader) mma_commit(&bars->o_full);
-      } while (false);
+        if (!ok) break;
+        if (leader) mma_commit(&bars->o_full);
+        g += n;
+      }
       if (issued) {
         if (leader) mma_commit(&bars->done);
         const unsigned long long t0 = globaltimer();
@@ -314,14 +365,22 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int t = (warp >= 8) ? 1 : 0;
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    uint32_t gs = 0;  // S blocks of this tile seen (s_full parity)
+    uint32_t ui = 0;
+    for (;; ++ui) {
+    const int u = unit_at(ui);
+    if (u >= num_units || !ok) break;
+    int b, h, m0, n0, n1;
+    decode(u, b, h, m0, n0, n1);
     const int qrow = m0 + t * kBM + row_in_tile;
     const int n_t = t == 0 ? n0 : n1;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     float m_run = -INFINITY;  // running max in log2 units (possibly stale)
     float l_run = 0.f;
-    bool ok = true;
     for (int j = 0; j < n_t; ++j) {
-      if (!mbar_wait(&bars->s_full[t], j & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) { ok = false; break; }
+      if (!mbar_wait(&bars->s_full[t], gs & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) { ok = false; break; }
+      ++gs;
       tc_fence_after();
       // All four 32-column loads in flight, then one wait; the empty asm
       // statements pin every use of the loaded registers after the wait.
@@ -423,46 +482,55 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[t]);
     }
-    if (ok && mbar_wait(&bars->o_full, 0, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
+    if (!ok || !mbar_wait(&bars->o_full, ui & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
+      ok = false;
+      break;
+    }
+    {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      // O rows -> swizzled staging in the (now idle) K/V ring -> TMA stores of
-      // one 32-row block per warp; rows >= S are clipped by the TMA unit.
-      uint8_t* stg = sK + (warp - 4) * (32 * D * 2);
+      // O rows -> swizzled staging (one atom-wide 32-row block per warp) -> TMA
+      // store; rows >= S are clipped by the TMA unit. One atom at a time.
+      uint8_t* stg = sO + (warp - 4) * Cfg::kOutStageBytes;
       const int swz = ((lane * Cfg::kAtomBytes) >> 7) & (Cfg::kAtomBytes / 16 - 1);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tO[t] + lane_off + c * 32, r);
-        tmem_ld_wait();
-        // 32 columns = 64 bytes = 4 chunks of 16 B, inside atom a = (c*32)/kAtom
-        const int col0 = c * 32;
-        uint8_t* atom = stg + (col0 / Cfg::kAtom) * (32 * Cfg::kAtomBytes);
-        const int chunk0 = (col0 % Cfg::kAtom) * 2 / 16;
+      for (int at = 0; at < Cfg::kNumAtoms; ++at) {
+        if (lane == 0) bulk_wait_group_read<0>();  // previous store has read the buffer
+        __syncwarp();
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint32_t w[4];
+        for (int c = 0; c < Cfg::kAtom / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO[t] + lane_off + at * Cfg::kAtom + c * 32, r);
+          tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float f0 = __uint_as_float(r[v * 8 + 2 * e]) * inv;
-            const float f1 = __uint_as_float(r[v * 8 + 2 * e + 1]) * inv;
-            w[e] = BF16 ? pack_bf162(f0, f1) : pack_half2(f0, f1);
+          for (int v = 0; v < 4; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float f0 = __uint_as_float(r[v * 8 + 2 * e]) * inv;
+              const float f1 = __uint_as_float(r[v * 8 + 2 * e + 1]) * inv;
+              w[e] = BF16 ? pack_bf162(f0, f1) : pack_half2(f0, f1);
+            }
+            *reinterpret_cast<uint4*>(stg + lane * Cfg::kAtomBytes + (((c * 4 + v) ^ swz) * 16)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
           }
-          *reinterpret_cast<uint4*>(atom + lane * Cfg::kAtomBytes + (((chunk0 + v) ^ swz) * 16)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (at == Cfg::kNumAtoms - 1) {
+          // every TMEM read of O is done: the next unit's first P.V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->o_empty);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(stg, &tmO, at * Cfg::kAtom, m0 + t * kBM + quarter * 32, h, b);
+          bulk_commit_group();
         }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        for (int at = 0; at < Cfg::kNumAtoms; ++at)
-          tma_store_4d(stg + at * (32 * Cfg::kAtomBytes), &tmO, at * Cfg::kAtom,
-                       m0 + t * kBM + quarter * 32, h, b);
-        bulk_commit_group();
-        bulk_wait_group<0>();
-      }
-      __syncwarp();
     }
+    }
+    if (lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -498,12 +566,16 @@ int launch(const void* q, const void* k, const void* v, void* o, long long B, lo
   auto kern = fa_sm100_kernel<D, BF16>;
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem));
   const int num_qblk = (int)((S + 2 * kBM - 1) / (2 * kBM));
-  const long long grid = (long long)num_qblk * B * H;
-  if (grid >= (1LL << 31)) {
+  const long long units = (long long)num_qblk * B * H;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long grid = units < sms ? units : sms;  // persistent: one CTA per SM
+  if (units >= (1LL << 31)) {
     set_error("b2_fa_fwd: grid too large");
     return B2_EINVAL;
   }
-  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, st>>>(tm[0], tm[1], tm[2], tmo, (int)H, (int)S, num_qblk,
+  kern<<<(unsigned)grid, kThreads, Cfg::kSmem, st>>>(tm[0], tm[1], tm[2], tmo, (int)H, (int)(B * H), (int)S, num_qblk,
                                                       sm_scale * kLog2e, causal);
   B2_CHECK_LAUNCH();
   return B2_OK;
