@@ -434,15 +434,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const f2_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
         float x0, x1, p0, p1;
         f2_unpack(x2, x0, x1);
-#if defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 4
-        if (!((i & 7) == 2 || (i & 7) == 5 || (i & 7) == 7)) {
-#elif defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 5
-        if ((i & 3) != 3) {
-#elif defined(B2_FA_EXPERIMENT) && B2_FA_EXPERIMENT == 6
-        if ((i & 7) != 7) {
-#else
         if ((i & 7) < 5) {
-#endif
           p0 = ex2(x0);
           p1 = ex2(x1);
         } else {
