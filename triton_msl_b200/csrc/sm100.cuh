@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) building blocks in inline PTX: mbarriers with bounded
-// waits, TMA tile loads (no cluster multicast anywhere in this library),
+// waits, TMA tile loads (each CTA loads its own tiles; no cross-CTA broadcast),
 // tcgen05 TMEM allocation / MMA / commit / load / store, and the shared-memory
 // matrix descriptors the tensor cores read.
 //
