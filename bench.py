@@ -318,6 +318,32 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic):
     from triton_msl_b200 import workloads as W
     out = {}
     steps = max(3, min(args.steps, 10))
+    # the other attention configs of BASELINE (head dims 64 / 32, bf16, fp32)
+    for cfg, kw in ((W.FA_F16_CAUSAL_D64, {}), (W.FA_F16_CAUSAL_D32, {}),
+                    (W.FAConfig("fa_bf16_causal_B4_H16_S2048_D128", 4, 16, 2048, 128, True,
+                                torch.bfloat16, 0.5), {}),
+                    (W.FA_F32, {"sm_scale": 1 / 8})):
+        q, k, v = W.fa_inputs(cfg, device=dev, seed=rank)
+        fn = lambda: b2.flash_attn_fwd(q, k, v, causal=cfg.causal, **kw)
+        fn()
+        kname = b2.last_kernel()
+        ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+        ach = cfg.flops() / (ms / 1e3) / 1e12
+        out[cfg.name] = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                         "kernel": kname,
+                         "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s",
+                                              "tensor", traffic, 1, peak_kind)}
+        del q, k, v
+    g32 = W.GEMM_F32
+    a32, b32, _ = W.gemm_inputs(g32, device=dev, seed=rank)
+    fn = lambda: b2.gemm(a32, b32)
+    fn()
+    kname = b2.last_kernel()
+    ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+    out[g32.name] = {"value": round(world * g32.flops() / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                     "ms": round(ms, 4), "kernel": kname,
+                     "note": "fp32 FFMA path (1e-4 bound); B200 dense fp32 is ~80 TFLOP/s nominal"}
+    del a32, b32
     g = W.GEMM_F16
     a, bm, bias = W.gemm_inputs(g, device=dev, seed=rank)
     fn = lambda: b2.gemm(a, bm, bias, "relu", torch.float16)
@@ -347,6 +373,60 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic):
     return out
 
 
+def run_scale(args, world, rank, local):
+    """a fixed total problem split across the ranks with no
+    collective (strong scaling). scale-fa: FA bf16 causal [64,32,8192,128] by
+    (batch, head); scale-gemm: GEMM bf16 65536x16384x16384 by 128-row M-tiles
+    (B replicated). Each rank builds only its own shard, on its own GPU."""
+    import math
+    import triton_msl_b200 as b2
+    from triton_msl_b200 import shard, workloads as W
+    dev = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_kind = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    if args.config == "scale-fa":
+        cfg = W.FA_BF16_SCALE
+        lo, hi = shard.unit_range(cfg.B * cfg.H, world, rank)
+        n = hi - lo
+        q, k, v = ((torch.randn((1, n, cfg.S, cfg.D), generator=g, device=dev) * cfg.std)
+                   .to(cfg.dtype) for _ in range(3))
+        fn = lambda: b2.flash_attn_fwd(q, k, v, causal=True)
+        flops_local = cfg.flops() * n / (cfg.B * cfg.H)
+        total = cfg.flops()
+        metric, workload = "fa_fwd_bf16_causal_d128_tflops", cfg.name
+        conf = {"B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D, "causal": True,
+                "units_this_rank": n}
+    else:
+        cfg = W.GEMM_BF16_SCALE
+        lo, hi = shard.unit_range(cfg.M, world, rank, align=128)
+        s_ = 1.0 / math.sqrt(cfg.K)
+        a = (torch.randn((hi - lo, cfg.K), generator=g, device=dev) * s_).to(cfg.dtype)
+        bm = (torch.randn((cfg.K, cfg.N), generator=g, device=dev) * s_).to(cfg.dtype)
+        fn = lambda: b2.gemm(a, bm)
+        flops_local = 2.0 * (hi - lo) * cfg.N * cfg.K
+        total = cfg.flops()
+        metric, workload = "gemm_bf16_tflops", cfg.name
+        conf = {"M": cfg.M, "N": cfg.N, "K": cfg.K, "rows_this_rank": hi - lo}
+    fn()
+    kname = b2.last_kernel()
+    times = time_launches(fn, args.steps, args.warmup, flush, world)
+    ms = max_over_ranks(statistics.mean(times), world)
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": metric, "value": round(total / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": workload, **conf, "parallelism": f"shards x{world}, no collective",
+                   "l2": "flushed between timed launches (256 MB write)"},
+        "roofline": roofline(kname, flops_local / (ms / 1e3) / 1e12, float(peaks["bf16_tflops"]),
+                             "TFLOP/s", "tensor", {}, 1, peak_kind),
+        "gpu_launches": args.steps,
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,6 +435,8 @@ def main():
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--headline-only", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--config", default="headline", choices=["headline", "scale-fa", "scale-gemm"],
+                    help="headline: BASELINE configs[1] (+ extras); scale-*: BASELINE config 5")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -362,6 +444,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.config != "headline":
+            run_scale(args, world, rank, local)
         else:
             run_b2(args, world, rank, local)
     finally:
