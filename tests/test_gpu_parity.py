@@ -280,3 +280,45 @@ def test_row_config4_full_size_properties():
 
 def test_device_status_clean():
     assert b2.device_status(0) == 0
+
+
+@pytest.mark.parametrize("D", [128, 64, 32])
+def test_fa_config2_full_size_sampled(D):
+    """BASELINE config 2 at full size ([4,16,2048,D] fp16 causal, N(0,1)*0.5),
+    checked on sampled (batch, head) slices against the oracle."""
+    cfg = W.FAConfig("c2", 4, 16, 2048, D, True, torch.float16, 0.5)
+    q, k, v = W.fa_inputs(cfg, device=DEV, seed=0)
+    o = b2.flash_attn_fwd(q, k, v, causal=True)
+    assert b2.last_kernel() == "fa_sm100"
+    for bb, hh in ((0, 0), (1, 7), (3, 15)):
+        sl = (slice(bb, bb + 1), slice(hh, hh + 1))
+        ref = O.ref_attention(q[sl].cpu(), k[sl].cpu(), v[sl].cpu(), True)
+        _check(o[sl], ref, torch.float16)
+
+
+def test_fa_config5_full_size_sampled():
+    """BASELINE config 5 attention at full size ([64,32,8192,128] bf16 causal),
+    sampled heads against the oracle plus a finiteness check over all of O."""
+    cfg = W.FA_BF16_SCALE
+    g = torch.Generator(device=DEV).manual_seed(0)
+    q, k, v = ((torch.randn((cfg.B, cfg.H, cfg.S, cfg.D), generator=g, device=DEV) * cfg.std)
+               .to(cfg.dtype) for _ in range(3))
+    o = b2.flash_attn_fwd(q, k, v, causal=True)
+    assert b2.last_kernel() == "fa_sm100"
+    assert torch.isfinite(o).all()
+    for bb, hh in ((0, 0), (63, 31)):
+        sl = (slice(bb, bb + 1), slice(hh, hh + 1))
+        ref = O.ref_attention(q[sl].cpu(), k[sl].cpu(), v[sl].cpu(), True)
+        _check(o[sl], ref, torch.bfloat16)
+
+
+def test_gemm_config5_full_size_sampled():
+    """BASELINE config 5 GEMM at full size (65536 x 16384 x 16384 bf16), sampled
+    row blocks against the fp32 oracle."""
+    cfg = W.GEMM_BF16_SCALE
+    a, b, _ = W.gemm_inputs(cfg, device=DEV, seed=0)
+    c = b2.gemm(a, b)
+    assert b2.last_kernel() == "gemm_sm100"
+    for r0 in (0, 32768 + 64, 65536 - 128):
+        ref = O.ref_gemm(a[r0:r0 + 128].cpu(), b.cpu(), out_dtype=torch.float32)
+        _check(c[r0:r0 + 128], ref, torch.bfloat16)
