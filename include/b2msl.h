@@ -52,6 +52,8 @@ extern "C" {
 #define B2_ACT_GELU 2      /* exact erf GELU */
 #define B2_ACT_GELU_TANH 3 /* tanh-approximated GELU */
 #define B2_ACT_SILU 4
+#define B2_ACT_SOFTMAX 5   /* softmax over each output row (fused matmul -> row softmax,
+                              reference _lowerer_templates.py:1515-1728); needs N <= 256 */
 
 /* row operations (b2_row_op) */
 #define B2_ROW_SOFTMAX 0

@@ -62,6 +62,10 @@ def ref_gemm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor] = No
         c = torch.nn.functional.gelu(c, approximate="tanh")
     elif activation == "silu":
         c = torch.nn.functional.silu(c)
+    elif activation == "softmax":
+        # fused matmul -> row softmax (reference _lowerer_templates.py:1515-1728,
+        # checked there against torch.softmax(a @ b, dim=1))
+        c = torch.softmax(c, dim=-1)
     elif activation != "none":
         raise ValueError(activation)
     return c.to(out_dtype or a.dtype)

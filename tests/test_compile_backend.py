@@ -110,3 +110,15 @@ def test_compiled_block_matches_eager_on_gpu():
         else:
             err = (g.float() - r.float()).abs().max().item() / max(r.float().abs().max().item(), 1e-6)
             assert err < 1e-2
+
+
+class MatmulSoftmax(nn.Module):
+    def forward(self, a, b):
+        return torch.softmax(a @ b, dim=-1)
+
+
+def test_rewrites_matmul_softmax_into_gemm_epilogue():
+    tags = _rewrite_all(MatmulSoftmax(), torch.randn(64, 32), torch.randn(32, 128))
+    assert "matmul+softmax" in tags
+    tags = _rewrite_all(MatmulSoftmax(), torch.randn(64, 32), torch.randn(32, 512))
+    assert "matmul+softmax" not in tags    # N > 256: separate softmax

@@ -322,3 +322,27 @@ def test_gemm_config5_full_size_sampled():
     for r0 in (0, 32768 + 64, 65536 - 128):
         ref = O.ref_gemm(a[r0:r0 + 128].cpu(), b.cpu(), out_dtype=torch.float32)
         _check(c[r0:r0 + 128], ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(512, 256, 512), (300, 200, 136), (128, 64, 64)])
+def test_gemm_softmax_epilogue(dtype, M, N, K):
+    """Fused matmul -> row softmax (reference _lowerer_templates.py:1515-1728)."""
+    a = _rand((M, K), dtype, 71, 1.0)
+    b = _rand((K, N), dtype, 72, 1.0 / math.sqrt(K))
+    bias = _rand((N,), torch.float32, 73, 0.3)
+    c = b2.gemm(a.to(DEV), b.to(DEV), bias.to(DEV), "softmax", torch.float32)
+    assert b2.last_kernel() == "gemm_sm100"
+    ref = O.ref_gemm(a, b, bias, "softmax", torch.float32)
+    _check(c, ref, dtype)
+    assert (c.sum(-1) - 1).abs().max().item() < 1e-4
+
+
+def test_gemm_softmax_epilogue_fp32_and_limits():
+    a = _rand((100, 64), torch.float32, 74)
+    b = _rand((64, 96), torch.float32, 75, 0.125)
+    c = b2.gemm(a.to(DEV), b.to(DEV), None, "softmax")
+    assert b2.last_kernel() == "gemm_simt+row_softmax"
+    _check(c, O.ref_gemm(a, b, None, "softmax"), torch.float32)
+    with pytest.raises(b2.B2Unsupported):
+        b2.gemm(a.to(DEV), _rand((64, 300), torch.float32, 76).to(DEV), None, "softmax")

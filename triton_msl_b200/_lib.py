@@ -19,7 +19,7 @@ LIB_PATH = Path(os.environ.get("B2MSL_LIBRARY", PKG / "libb2msl.so"))
 
 B2_OK, B2_EINVAL, B2_EUNSUPPORTED, B2_ELAUNCH, B2_ETIMEOUT = 0, -1, -2, -3, -4
 B2_F32, B2_F16, B2_BF16, B2_I64 = 0, 1, 2, 3
-ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
+ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4, "softmax": 5}
 ROW_OPS = {"softmax": 0, "layernorm": 1, "rmsnorm": 2, "sum": 3, "max": 4,
            "argmax": 5, "min": 6, "argmin": 7}
 

@@ -12,7 +12,8 @@ Dynamo captures and replaced by calls to the custom ops:
 * ``F.scaled_dot_product_attention(q, k, v[, is_causal, scale])`` and the
   explicit ``softmax(q @ k.transpose(-2, -1) * s) @ v`` chain -> ``flash_attn_fwd``
 * ``F.linear(x, w[, b])`` / ``torch.matmul`` / ``@`` / ``torch.addmm`` on 2-D
-  operands, with a following ``relu`` / ``gelu`` / ``silu`` folded in -> ``gemm``
+  operands, with a following ``relu`` / ``gelu`` / ``silu`` or a last-dim
+  ``softmax`` (N <= 256, the fused matmul-softmax) folded in -> ``gemm``
 * ``softmax(x, dim=-1)``, ``F.layer_norm`` over the last dim, ``F.rms_norm``
   over the last dim, ``sum / amax / amin / argmax / argmin(dim=-1)`` -> row ops
 
@@ -156,7 +157,28 @@ class Rewriter:
             return u, _ACTS[_target_key(u)]
         if u.op == "call_function" and u.target is F.gelu and u.kwargs.get("approximate", "none") == "tanh":
             return u, "gelu_tanh"
+        # matmul -> row softmax (the reference's fused matmul-softmax template),
+        # when one output tile covers a row
+        if _in(u, _SOFTMAX) and u.args and u.args[0] is node and u.kwargs.get("dtype") is None:
+            v = _val(node)
+            if v is not None and _is_last_dim(_arg(u, 1, "dim"), v) and v.shape[-1] <= 256:
+                return u, "softmax"
         return None, None
+
+    def _fusable_producer(self, x: fx.Node) -> bool:
+        """x is a 2-D matmul / linear / addmm this pass will rewrite to a GEMM whose
+        output rows fit one tile (N <= 256)."""
+        v = _val(x)
+        if v is None or v.shape[-1] > 256:
+            return False
+        ac = self.allow_cpu
+        if _in(x, _MATMUL) and len(x.args) == 2:
+            return _ok_tensor(x.args[0], ac, 2) and _ok_tensor(x.args[1], ac, 2)
+        if _in(x, _LINEAR):
+            return _ok_tensor(x.args[0], ac) and _ok_tensor(x.args[1], ac, 2)
+        if _target_key(x) is torch.addmm and len(x.args) == 3:
+            return all(_ok_tensor(a, ac) for a in x.args)
+        return False
 
     def run(self) -> List[str]:
         # Consumers first, so a chain (softmax inside explicit attention, an
@@ -221,8 +243,10 @@ class Rewriter:
             return
         # ---- row family
         if _in(node, _SOFTMAX):
-            x = node.args[0] if node.op == "call_function" else node.args[0]
+            x = node.args[0]
             dim = _arg(node, 1, "dim")
+            if isinstance(x, fx.Node) and len(x.users) == 1 and self._fusable_producer(x):
+                return  # the producing matmul absorbs it as a softmax epilogue
             if _ok_tensor(x, ac) and _is_last_dim(dim, _val(x)) and node.kwargs.get("dtype") is None:
                 self._replace(node, b2ops.row_softmax, (x,), "softmax")
             return

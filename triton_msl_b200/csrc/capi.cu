@@ -134,7 +134,7 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
               out_dtype);
     return B2_EINVAL;
   }
-  if (act < B2_ACT_NONE || act > B2_ACT_SILU) {
+  if (act < B2_ACT_NONE || act > B2_ACT_SOFTMAX) {
     set_error("b2_gemm: unknown activation %d", act);
     return B2_EINVAL;
   }
@@ -143,9 +143,31 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
     set_error("b2_gemm: null pointer argument");
     return B2_EINVAL;
   }
+  if (act == B2_ACT_SOFTMAX && N > 256) {
+    set_error("b2_gemm: the row-softmax epilogue needs N <= 256 (one output tile per row); got N=%lld",
+              (long long)N);
+    return B2_EUNSUPPORTED;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int rc;
-  if (device_is_sm100() && strides[5] == 1 && gemm_sm100_eligible(A, Bm, M, N, K, strides, in_dtype)) {
+  const bool tc = device_is_sm100() && strides[5] == 1 &&
+                  gemm_sm100_eligible(A, Bm, M, N, K, strides, in_dtype);
+  if (act == B2_ACT_SOFTMAX && !tc) {
+    // CUDA-core path: fp32 logits into C, then the row-softmax kernel in place
+    // (exact only when C holds fp32).
+    if (out_dtype != B2_F32 || strides[5] != 1) {
+      set_error("b2_gemm: row-softmax epilogue off the tensor-core path needs fp32, unit-stride C");
+      return B2_EUNSUPPORTED;
+    }
+    rc = gemm_simt_launch(A, Bm, bias, C, M, N, K, strides, alpha, B2_ACT_NONE, in_dtype, bias_dtype,
+                          out_dtype, st);
+    if (rc != B2_OK) return rc;
+    rc = row_op_launch(B2_ROW_SOFTMAX, C, nullptr, nullptr, C, M, N, strides[4], strides[4], 0.f,
+                       B2_F32, nullptr, 0, st);
+    if (rc == B2_OK) t_kernel = "gemm_simt+row_softmax";
+    return rc;
+  }
+  if (tc) {
     rc = gemm_sm100_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
                            out_dtype, st);
     if (rc == B2_OK) t_kernel = "gemm_sm100";

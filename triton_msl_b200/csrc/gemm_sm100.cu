@@ -254,6 +254,39 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       const int row = mb * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
       TO* crow = C + (long long)row * ldc;
+      // Row-softmax epilogue (N <= kBN, so this tile holds whole rows): two
+      // read passes over the accumulator for the row max and the sum of
+      // exponentials, then the chunk loop below writes exp(x - max) / sum.
+      float sm_max = 0.f, sm_inv = 0.f;
+      if (act == B2_ACT_SOFTMAX) {
+        constexpr float kLog2e = 1.4426950408889634f;
+        float mloc = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32 && c * 32 < N; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = fmaf(__uint_as_float(r[j]), alpha, bias ? tb_bias[c * 32 + j] : 0.f);
+            if (c * 32 + j < N) mloc = fmaxf(mloc, x);
+          }
+        }
+        float l = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32 && c * 32 < N; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = fmaf(__uint_as_float(r[j]), alpha, bias ? tb_bias[c * 32 + j] : 0.f);
+            if (c * 32 + j < N) l += exp2f((x - mloc) * kLog2e);
+          }
+        }
+        sm_max = mloc;
+        sm_inv = 1.f / l;
+      }
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
@@ -275,6 +308,10 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = apply_act(fmaf(__uint_as_float(r[j]), alpha, bv[j]), act);
+        if (act == B2_ACT_SOFTMAX) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = exp2f((f[j] - sm_max) * 1.4426950408889634f) * sm_inv;
+        }
         if (use_tma_store) {
           // Row `lane` of a 32x32 block -> swizzled staging -> one TMA store
           // per warp (rows >= M and columns >= N are clipped by the TMA unit).

@@ -142,7 +142,11 @@ def _(a, b, bias, activation, out_dtype, alpha):
 def gemm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor] = None,
          activation: str = "none", out_dtype: Optional[torch.dtype] = None,
          alpha: float = 1.0) -> torch.Tensor:
-    """c = activation(alpha * (a @ b) + bias[None, :]) with fp32 accumulation."""
+    """c = activation(alpha * (a @ b) + bias[None, :]) with fp32 accumulation.
+
+    activation: none / relu / gelu / gelu_tanh / silu, or softmax (a softmax over
+    each output row, the reference's fused matmul + row-softmax; N <= 256).
+    """
     return torch.ops.b2msl.gemm(a, b, bias, activation, out_dtype, float(alpha))
 
 
