@@ -35,6 +35,13 @@ __device__ uint32_t g_fa_status;
 constexpr int kBM = 128;      // query rows per tile
 constexpr int kBN = 128;      // keys per block
 constexpr int kThreads = 384; // 12 warps
+// Register split (setmaxnreg): warpgroup 0 (TMA, MMA, two idle warps) gives
+// registers to the two softmax warpgroups, which hold a 128-key row of S and
+// its packed P per thread. The sum must fit the block's launch allocation,
+// kThreads x kLaunchRegs; the host checks the compiled register count.
+constexpr int kRegsProducer = 56, kRegsSoftmax = 224, kLaunchRegs = 168;
+static_assert(128 * (kRegsProducer + 2 * kRegsSoftmax) <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -206,8 +213,11 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
 
+  // Each role branch executes its own setmaxnreg, so the compiler sees one
+  // register budget per region.
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
     if (lane == 0) {
       bool ok = true;
       uint32_t g = 0;   // K/V blocks issued by this CTA (ring position)
@@ -255,6 +265,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
     // The whole warp runs the issue loop (so loop-invariant operands stay
     // warp-uniform) and one elected lane issues each tcgen05 instruction.
     {
@@ -362,6 +373,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   } else if (warp >= 4) {
     // ------------------------------------------------- softmax / correction
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     const int t = (warp >= 8) ? 1 : 0;
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
@@ -524,6 +536,8 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     }
     if (lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsProducer));
   }
 
   tc_fence_before();
@@ -558,6 +572,17 @@ int launch(const void* q, const void* k, const void* v, void* o, long long B, lo
   }
   auto kern = fa_sm100_kernel<D, BF16>;
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem));
+  {
+    // setmaxnreg.inc waits until the block's register pool can serve it, so
+    // only launch when the compiled allocation covers the split.
+    cudaFuncAttributes fa;
+    B2_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs < kLaunchRegs) {
+      set_error("b2_fa_fwd: kernel compiled with %d registers/thread, register split needs %d",
+                fa.numRegs, kLaunchRegs);
+      return B2_ELAUNCH;
+    }
+  }
   const int num_qblk = (int)((S + 2 * kBM - 1) / (2 * kBM));
   const long long units = (long long)num_qblk * B * H;
   int dev = 0, sms = 148;
