@@ -179,13 +179,15 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
   constexpr int RPB = BLOCK / TPR;  // rows per block
   static_assert(TPR <= 32 || RPB == 1, "multi-row blocks need TPR <= 32");
   __shared__ float red_v[32];
-  __shared__ int red_i[32];
+  __shared__ float red_av[2][32];  // argmax / argmin: one buffer per row parity,
+  __shared__ int red_ai[2][32];    // so consecutive rows need no extra barrier
 
   const int sub = threadIdx.x % TPR;          // thread index inside the row
   const int rloc = threadIdx.x / TPR;         // row slot inside the block
   const float inv_cols = 1.f / (float)cols;
 
-  for (long long row0 = (long long)blockIdx.x * RPB; row0 < rows; row0 += (long long)gridDim.x * RPB) {
+  int parity = 0;
+  for (long long row0 = (long long)blockIdx.x * RPB; row0 < rows; row0 += (long long)gridDim.x * RPB, parity ^= 1) {
     const long long row = row0 + rloc;
     const bool row_ok = row < rows;
     const T* xr = x + (row_ok ? row : 0) * ldx;
@@ -214,27 +216,47 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
       if (row_ok && sub == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
     } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
       constexpr bool MAXI = OP == B2_ROW_ARGMAX;
-      // This thread visits its columns in increasing order, so a strict
-      // comparison keeps the earliest of equal values and the first NaN;
-      // 32-bit indices (rows are < 2^31 columns) until the int64 store.
-      float bv = MAXI ? -INFINITY : INFINITY;
-      int bi = 0x7fffffff;
+      // One independent scan per vector lane j (EPV chains, so the compare /
+      // select latency overlaps); each chain visits its columns in increasing
+      // order, so a strict comparison keeps the earliest of equal values and
+      // the first NaN, and arg_better (ties -> lower index) merges the chains
+      // exactly. 32-bit indices (rows are < 2^31 columns) until the int64 store.
+      float cv[EPV];
+      int ck[EPV];
 #pragma unroll
-      for (int i = 0; i < VPT; ++i)
+      for (int j = 0; j < EPV; ++j) {
+        cv[j] = MAXI ? -INFINITY : INFINITY;
+        ck[j] = 0x7fffffff;
+      }
+      // columns grow with i, so a thread without a first vector has none
+      if (ok[0]) {
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) {
+          cv[j] = v[0][j];
+          ck[j] = sub * EPV + j;
+        }
+      }
+#pragma unroll
+      for (int i = 1; i < VPT; ++i)
         if (ok[i]) {
 #pragma unroll
           for (int j = 0; j < EPV; ++j) {
             const float x = v[i][j];
             const int ci = (sub + i * TPR) * EPV + j;
-            const bool take = (MAXI ? x > bv : x < bv) || (x != x && bv == bv) || bi == 0x7fffffff;
-            bv = take ? x : bv;
-            bi = take ? ci : bi;
+            // x beats the chain's best: strictly better, or a NaN against a
+            // number (NaN is the extreme value)
+            const bool take = (MAXI ? !(x <= cv[j]) : !(x >= cv[j])) && cv[j] == cv[j];
+            cv[j] = take ? x : cv[j];
+            ck[j] = take ? ci : ck[j];
           }
         }
-      if constexpr (TPR > 32) __syncthreads();
-      row_reduce_arg<TPR, MAXI>(bv, bi, red_v, red_i);
+      float bv = cv[0];
+      int bi = ck[0];
+#pragma unroll
+      for (int j = 1; j < EPV; ++j)
+        if (arg_better<MAXI>(cv[j], ck[j], bv, bi)) { bv = cv[j]; bi = ck[j]; }
+      row_reduce_arg<TPR, MAXI>(bv, bi, red_av[parity], red_ai[parity]);
       if (row_ok && sub == 0) reinterpret_cast<long long*>(out)[row] = (long long)bi;
-      if constexpr (TPR > 32) __syncthreads();
     } else if constexpr (OP == B2_ROW_SOFTMAX) {
       float m = -INFINITY;
 #pragma unroll
@@ -535,6 +557,19 @@ int dispatch_reg(const void* x, const void* w, const void* b, void* out, long lo
   constexpr int EPV = Vec<T>::N;
   constexpr int V16 = 16 / EPV;  // vectors per thread for 16 elements
   const int per16 = (cols + 15) / 16;
+  if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+    // index tracking doubles the cross-thread reduction: 32 elements per
+    // thread halve the threads per row (65536x4096 fp32 on B200: 0.86 -> 0.96
+    // of the measured HBM copy bandwidth)
+    if (per16 > 64 && per16 <= 2048) {
+      const int per32 = (cols + 31) / 32;
+      if (per32 <= 64) return launch_reg<T, OP, 64, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 128) return launch_reg<T, OP, 128, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 256) return launch_reg<T, OP, 256, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 512) return launch_reg<T, OP, 512, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      return launch_reg<T, OP, 1024, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    }
+  }
   if (per16 <= 8) return launch_reg<T, OP, 8, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
   if (per16 <= 16) return launch_reg<T, OP, 16, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
   if (per16 <= 32) return launch_reg<T, OP, 32, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
