@@ -150,12 +150,96 @@ def test_gemm_k_major_b_linear_layout():
 
 
 def test_gemm_config3_prime_fp32():
-    """fp32 inputs at 2048^3 (BASELINE config 3'), max-abs 1e-4."""
+    """fp32 inputs at 2048^3 (BASELINE config 3'), max-abs 1e-4, on the 3xTF32
+    tensor-core path."""
     cfg = W.GEMM_F32
     a, b, _ = W.gemm_inputs(cfg, seed=0)
     c = b2.gemm(a.to(DEV), b.to(DEV))
-    assert b2.last_kernel() == "gemm_simt"
+    assert b2.last_kernel() == "gemm_sm100_tf32x3"
     _check(c, O.ref_gemm(a, b), torch.float32)
+
+
+def _gemm_no_workspace(a, b, bias=None, act="none"):
+    """b2_gemm through the C ABI with no workspace: fp32 takes the FMA path."""
+    from triton_msl_b200 import _lib
+    c = torch.empty((a.shape[0], b.shape[1]), dtype=torch.float32, device=DEV)
+    st = _lib.lib().b2_gemm(a.data_ptr(), b.data_ptr(), bias.data_ptr() if bias is not None else None,
+                            c.data_ptr(), a.shape[0], b.shape[1], a.shape[1],
+                            _lib.i64_array([*a.stride(), *b.stride(), *c.stride()]), 1.0,
+                            _lib.ACT[act], _lib.B2_F32, _lib.B2_F32, _lib.B2_F32, None, 0,
+                            torch.cuda.current_stream().cuda_stream)
+    _lib.check("b2_gemm", st)
+    return c
+
+
+def test_gemm_fp32_fma_path_without_workspace():
+    a = _rand((257, 129), torch.float32, 81)
+    b = _rand((129, 95), torch.float32, 82, 1 / math.sqrt(129))
+    bias = _rand((95,), torch.float32, 83, 0.1)
+    c = _gemm_no_workspace(a.to(DEV), b.to(DEV), bias.to(DEV), "gelu")
+    assert b2.last_kernel() == "gemm_simt"
+    _check(c, O.ref_gemm(a, b, bias, "gelu"), torch.float32)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (129, 257, 33), (300, 200, 1000), (64, 512, 7),
+                                   (1000, 96, 520)])
+@pytest.mark.parametrize("b_layout", ["kn", "nk"])
+def test_gemm_tf32x3_shapes_layouts(M, N, K, b_layout):
+    """3xTF32: ragged M/N/K (K padded per segment), B as [K,N] or a transposed
+    [N,K] view (the split pass reads either), max-abs 1e-4 against fp32
+    (entries of C ~ N(0, 1))."""
+    s4 = K ** -0.25
+    a = _rand((M, K), torch.float32, 84, s4)
+    if b_layout == "kn":
+        b = _rand((K, N), torch.float32, 85, s4).to(DEV)
+    else:
+        b = _rand((N, K), torch.float32, 85, s4).to(DEV).t()
+    bias = _rand((N,), torch.float32, 86, 0.1)
+    c = b2.gemm(a.to(DEV), b, bias.to(DEV), "relu")
+    assert b2.last_kernel() == "gemm_sm100_tf32x3"
+    _check(c, O.ref_gemm(a, b.cpu(), bias, "relu"), torch.float32)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_gemm_tf32x3_low_precision_out(out_dtype):
+    a = _rand((200, 300), torch.float32, 87)
+    b = _rand((300, 160), torch.float32, 88, 1 / math.sqrt(300))
+    c = b2.gemm(a.to(DEV), b.to(DEV), None, "silu", out_dtype)
+    assert b2.last_kernel() == "gemm_sm100_tf32x3"
+    _check(c, O.ref_gemm(a, b, None, "silu", torch.float32), out_dtype)
+
+
+@pytest.mark.parametrize("K", [2048, 8192])
+def test_gemm_tf32x3_error_growth_with_k(K):
+    """The tensor core's fp32 accumulation loses about one unit in the last
+    place of the running sum per K=8 step, so the error grows with K and with
+    |C| (measured on B200: ~2.7e-5 of max|C| at K=2048, ~1.9e-4 at K=16384),
+    an order below plain TF32 and well inside 1e-4 for configs like BASELINE's
+    (A, B ~ N(0,1)/sqrt(K), |C| ~ 0.02: 2.3e-6 at 2048^3). Bound written here:
+    max-abs <= 5e-5 * (K / 2048) * max|C|."""
+    a = _rand((256, K), torch.float32, 89)
+    b = _rand((K, 256), torch.float32, 90, 1 / math.sqrt(K))
+    ref = a.double() @ b.double()
+    c = b2.gemm(a.to(DEV), b.to(DEV)).double().cpu()
+    bound = 5e-5 * (K / 2048) * ref.abs().max().item()
+    assert (c - ref).abs().max().item() <= bound
+
+
+def test_gemm_tf32x3_beats_plain_tf32_accuracy():
+    """The hi/lo split is what meets 1e-4: plain TF32 (torch with TF32 matmul
+    allowed) misses it on this input, 3xTF32 does not."""
+    a = _rand((256, 2048), torch.float32, 89)
+    b = _rand((2048, 256), torch.float32, 90)
+    ref = O.ref_gemm(a, b)
+    c = b2.gemm(a.to(DEV), b.to(DEV))
+    assert O.max_abs_err(c, ref) <= 0.05  # |C| ~ 180 here
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        plain = a.to(DEV) @ b.to(DEV)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert O.max_abs_err(plain, ref) > 10 * O.max_abs_err(c, ref)
 
 
 def test_gemm_odd_strides_fall_back_to_cuda_cores():
@@ -342,6 +426,9 @@ def test_gemm_softmax_epilogue_fp32_and_limits():
     a = _rand((100, 64), torch.float32, 74)
     b = _rand((64, 96), torch.float32, 75, 0.125)
     c = b2.gemm(a.to(DEV), b.to(DEV), None, "softmax")
+    assert b2.last_kernel() == "gemm_sm100_tf32x3"
+    _check(c, O.ref_gemm(a, b, None, "softmax"), torch.float32)
+    c = _gemm_no_workspace(a.to(DEV), b.to(DEV), None, "softmax")
     assert b2.last_kernel() == "gemm_simt+row_softmax"
     _check(c, O.ref_gemm(a, b, None, "softmax"), torch.float32)
     with pytest.raises(b2.B2Unsupported):

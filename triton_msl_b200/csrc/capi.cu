@@ -22,6 +22,9 @@ bool gemm_sm100_eligible(const void*, const void*, long long, long long, long lo
                          const int64_t*, int);
 int gemm_sm100_launch(const void*, const void*, const void*, void*, long long, long long,
                       long long, const int64_t*, float, int, int, int, int, cudaStream_t);
+size_t gemm_tf32x3_workspace(long long, long long, long long);
+int gemm_tf32x3_launch(const float*, const float*, const void*, void*, long long, long long,
+                       long long, const int64_t*, float, int, int, int, void*, cudaStream_t);
 size_t row_op_workspace(int, long long, long long);
 int row_op_launch(int, const void*, const void*, const void*, void*, long long, long long,
                   long long, long long, float, int, void*, size_t, cudaStream_t);
@@ -121,8 +124,6 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, i
 int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
             int64_t K, const int64_t strides[6], float alpha, int act, int in_dtype,
             int bias_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
-  (void)workspace;
-  (void)ws_bytes;
   clear_error();
   if (M < 0 || N < 0 || K < 0) {
     set_error("b2_gemm: invalid shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
@@ -150,8 +151,14 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int rc;
-  const bool tc = device_is_sm100() && strides[5] == 1 &&
-                  gemm_sm100_eligible(A, Bm, M, N, K, strides, in_dtype);
+  const bool sm100 = device_is_sm100();
+  // fp32 inputs: 3xTF32 on the tensor cores when the caller passed the
+  // workspace b2_query_workspace asked for, else fp32 FMA.
+  const size_t tf3_need = in_dtype == B2_F32 ? gemm_tf32x3_workspace(M, N, K) : 0;
+  const bool tf3 = sm100 && in_dtype == B2_F32 && strides[5] == 1 && tf3_need > 0 && workspace &&
+                   ws_bytes >= tf3_need && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0;
+  const bool tc = tf3 || (sm100 && strides[5] == 1 &&
+                          gemm_sm100_eligible(A, Bm, M, N, K, strides, in_dtype));
   if (act == B2_ACT_SOFTMAX && !tc) {
     // CUDA-core path: fp32 logits into C, then the row-softmax kernel in place
     // (exact only when C holds fp32).
@@ -167,7 +174,11 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
     if (rc == B2_OK) t_kernel = "gemm_simt+row_softmax";
     return rc;
   }
-  if (tc) {
+  if (tf3) {
+    rc = gemm_tf32x3_launch(reinterpret_cast<const float*>(A), reinterpret_cast<const float*>(Bm),
+                            bias, C, M, N, K, strides, alpha, act, bias_dtype, out_dtype, workspace, st);
+    if (rc == B2_OK) t_kernel = "gemm_sm100_tf32x3";
+  } else if (tc) {
     rc = gemm_sm100_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
                            out_dtype, st);
     if (rc == B2_OK) t_kernel = "gemm_sm100";
@@ -230,7 +241,7 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out, in
 size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3) {
   (void)a3;
   switch (kind) {
-    case 0: return 0;
+    case 0: return (a3 == B2_F32 && device_is_sm100()) ? gemm_tf32x3_workspace(a0, a1, a2) : 0;
     case 1: return row_op_workspace((int)a0, a1, a2);
     case 2: return 0;
     default: return 0;

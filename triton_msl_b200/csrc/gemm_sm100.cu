@@ -75,7 +75,9 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = r / gsize;
 }
 
-template <typename TO, bool B_MN>
+// TF32: operands are fp32 hi/lo splits laid out by tf32_split_kernel (both
+// K-major), 32 elements per 128-byte row, consumed by kind::tf32 MMAs.
+template <typename TO, bool B_MN, bool TF32>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int use_tma_store,
@@ -95,7 +97,9 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
   const int tiles = num_m * num_n;
-  const int nk = (K + kBK - 1) / kBK;
+  static_assert(!(TF32 && B_MN), "tf32 operands are K-major");
+  constexpr int kKE = TF32 ? 32 : kBK;  // K elements per 128-byte swizzle row
+  const int nk = (K + kKE - 1) / kKE;
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -138,14 +142,14 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             break;
           }
           mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
-          tma_load_2d(sA + stage * kABytes, &tmA, &bars->full[stage], kb * kBK, mb * kBM);
+          tma_load_2d(sA + stage * kABytes, &tmA, &bars->full[stage], kb * kKE, mb * kBM);
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < kBN / 64; ++j)
               tma_load_2d(sB + stage * kBBytes + j * (64 * kBK * 2), &tmB, &bars->full[stage],
                           nb * kBN + j * 64, kb * kBK);
           } else {
-            tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], kb * kBK, nb * kBN);
+            tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], kb * kKE, nb * kBN);
           }
           filled |= 1u << stage;
           if (++stage == kRing) {
@@ -200,7 +204,11 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const uint64_t ad = sdesc(a0 + k * 32, 16, 1024, kSwizzle128);
             const uint64_t bd = B_MN ? sdesc(b0 + k * 16 * 128, 64 * kBK * 2, 1024, kSwizzle128)
                                      : sdesc(b0 + k * 32, 16, 1024, kSwizzle128);
-            if (leader) mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            // 32 bytes of K per instruction: K=16 (f16/bf16) or K=8 (tf32)
+            if (leader) {
+              if (TF32) mma_tf32_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              else mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           issued = true;
           if (leader) mma_commit(&bars->empty[stage]);
@@ -385,14 +393,66 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   }
 }
 
+// ---------------------------------------------------------------- 3xTF32
+// fp32 GEMM on the tf32 tensor path with fp32-level accuracy: x = hi + lo with
+// hi = tf32(x) and lo = tf32(x - hi), and
+//   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
+// (the dropped A_lo.B_lo is ~2^-22 relative). The three products are one GEMM
+// over a tripled K: row r of the split operand holds [hi | hi | lo] for A and
+// [hi | lo | hi] for B (B transposed to K-major), each segment Kp = K rounded up
+// to 32 long and zero-padded, so the tensor-core kernel runs unchanged with
+// K' = 3 Kp.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// src[r, k] at src + r*sr + k*sk (R rows, K columns) -> dst[r, seg*Kp + k];
+// lo_seg (1 or 2) is the segment that receives lo. 32x32 tiles through shared
+// memory so both a row-major A and a [K, N] B read and write coalesced.
+__global__ void __launch_bounds__(256)
+tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long long sr, long long sk,
+                  float* __restrict__ dst, long long Kp, int lo_seg) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const long long r0 = (long long)blockIdx.y * 32, k0 = (long long)blockIdx.x * 32;
+  if (sk == 1) {
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const long long r = r0 + i, k = k0 + tx;
+      tile[i][tx] = (r < R && k < K) ? src[r * sr + k] : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const long long r = r0 + tx, k = k0 + i;
+      tile[tx][i] = (r < R && k < K) ? src[r * sr + k * sk] : 0.f;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = ty; i < 32; i += 8) {
+    const long long r = r0 + i;
+    if (r >= R) continue;
+    const float x = tile[i][tx];
+    const float hi = tf32_rna(x);
+    const float lo = tf32_rna(x - hi);
+    float* d = dst + r * 3 * Kp + k0 + tx;
+    d[0] = hi;
+    d[Kp] = lo_seg == 1 ? lo : hi;
+    d[2 * Kp] = lo_seg == 2 ? lo : hi;
+  }
+}
+
 int g_sms = 0;
 
-template <typename TO, bool B_MN>
+template <typename TO, bool B_MN, bool TF32 = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
            const void* bias, int bias_dt, void* C,
            long long M, long long N, long long K, long long ldc, float alpha, int act,
            uint32_t idesc, int vec_ok, cudaStream_t st) {
-  auto kern = gemm_sm100_kernel<TO, B_MN>;
+  auto kern = gemm_sm100_kernel<TO, B_MN, TF32>;
   const size_t smem = 1024 + EpiCfg<TO>::kRing * kStageBytes + EpiCfg<TO>::kEpiSmem + sizeof(GemmBarriers);
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   if (g_sms == 0) {
@@ -483,6 +543,81 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
     case B2_F32:
       return b_mn ? launch<float, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
                   : launch<float, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+  }
+  set_error("b2_gemm: unsupported out dtype %d", out_dt);
+  return B2_EINVAL;
+}
+
+size_t gemm_tf32x3_workspace(long long M, long long N, long long K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const long long Kp = (K + 31) / 32 * 32;
+  return (size_t)(M + N) * 3 * (size_t)Kp * sizeof(float);
+}
+
+int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C, long long M,
+                       long long N, long long K, const int64_t* s, float alpha, int act,
+                       int bias_dt, int out_dt, void* workspace, cudaStream_t st) {
+  if (M >= (1LL << 31) || N >= (1LL << 31) || 3 * ((K + 31) / 32 * 32) >= (1LL << 31)) {
+    set_error("b2_gemm: dims too large for the 3xTF32 path");
+    return B2_EINVAL;
+  }
+  if (s[5] != 1) {
+    set_error("b2_gemm: tensor-core path needs unit column stride in C");
+    return B2_EUNSUPPORTED;
+  }
+  const long long Kp = (K + 31) / 32 * 32, K3 = 3 * Kp;
+  float* Ap = reinterpret_cast<float*>(workspace);
+  float* Bp = Ap + (size_t)M * K3;
+  {
+    const dim3 blk(256);
+    tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)((M + 31) / 32)), blk, 0, st>>>(
+        A, M, K, s[0], s[1], Ap, Kp, 2);
+    B2_CHECK_LAUNCH();
+    // B[k, n] at B + k*s[2] + n*s[3]: rows of the split operand are n
+    tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)((N + 31) / 32)), blk, 0, st>>>(
+        B, N, K, s[3], s[2], Bp, Kp, 1);
+    B2_CHECK_LAUNCH();
+  }
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)K3, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K3 * 4};
+    const uint32_t box[2] = {32, kBM};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Ap, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K3, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)K3 * 4};
+    const uint32_t box[2] = {32, kBN};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Bp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+  }
+  const uint32_t idesc = idesc_tf32(kBM, kBN);
+  const int osz = dtype_size(out_dt);
+  const int vec_ok = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
+  if (bias == nullptr) bias_dt = B2_F32;
+  CUtensorMap tc;
+  int use_tma = 0;
+  if (vec_ok && s[4] >= N) {
+    const CUtensorMapDataType cdt = out_dt == B2_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : out_dt == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)s[4] * osz};
+    const uint32_t box[2] = {32, 32};
+    use_tma = encode_tmap(&tc, cdt, 2, C, dims, strides, box,
+                          osz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
+    clear_error();
+  }
+  if (!use_tma) memset(&tc, 0, sizeof(tc));
+  switch (out_dt) {
+    case B2_F16:
+      return launch<__half, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
+    case B2_BF16:
+      return launch<__nv_bfloat16, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
+    case B2_F32:
+      return launch<float, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;

@@ -118,12 +118,16 @@ def _gemm_impl(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor], a
     cout = _dtype_code(c, what)
     bdt = _dtype_code(bias, what) if bias is not None else _lib.B2_F32
     strides = [a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)]
+    L = _lib.lib()
     with torch.cuda.device(dev):
-        st = _lib.lib().b2_gemm(a.data_ptr(), b.data_ptr(),
-                                bias.data_ptr() if bias is not None else None, c.data_ptr(),
-                                M, N, K, _lib.i64_array(strides), float(alpha),
-                                _lib.ACT[activation], _dtype_code(a, what), bdt, cout,
-                                None, 0, _stream(dev))
+        # fp32 inputs run as 3xTF32 on the tensor cores with this scratch
+        ws_bytes = L.b2_query_workspace(0, M, N, K, _dtype_code(a, what))
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev) if ws_bytes else None
+        st = L.b2_gemm(a.data_ptr(), b.data_ptr(),
+                       bias.data_ptr() if bias is not None else None, c.data_ptr(),
+                       M, N, K, _lib.i64_array(strides), float(alpha),
+                       _lib.ACT[activation], _dtype_code(a, what), bdt, cout,
+                       ws.data_ptr() if ws is not None else None, ws_bytes, _stream(dev))
     _lib.check("b2_gemm", st)
     return c
 
