@@ -52,7 +52,7 @@ struct __align__(8) FaBarriers {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_full, o_empty;
+  uint64_t o_full[2], o_empty[2];  // per tile: O_t complete / O_t read out
   uint64_t q_empty;
   uint64_t done;
   uint32_t tmem_base;
@@ -192,8 +192,10 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 4);
     }
-    mbar_init(&bars->o_full, 1);
-    mbar_init(&bars->o_empty, 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->o_full[i], 1);
+      mbar_init(&bars->o_empty[i], 4);
+    }
     mbar_init(&bars->done, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -326,19 +328,22 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         if (leader) mma_commit(&bars->k_empty[g & 1]);
         if (n == 1 && leader) mma_commit(&bars->q_empty);
         issued = true;
-        // O_0 / O_1 still hold the previous unit's result until the softmax
-        // warps have read it.
-        if (!mbar_wait(&bars->o_empty, (ui & 1) ^ 1u, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
         for (int j = 0; j < n; ++j) {
           const uint32_t gj = g + j;
           const int vs = gj & 1;
           const uint32_t vph = (gj >> 1) & 1;
           if (!mbar_wait(&bars->v_full[vs], vph, abort_flag, &g_fa_status, DEV_TIMEOUT_TMA)) { ok = false; break; }
           if (j < n0) {
+            // O_0 holds the previous unit's result until tile 0's softmax warps
+            // have read it out
+            if (j == 0 && !mbar_wait(&bars->o_empty[0], (ui & 1) ^ 1u, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
             if (!mbar_wait(&bars->p_full[0], gs0 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
             tc_fence_after();
             pv(0, vs, j > 0);
             ++gs0;
+            // causal: tile 0 ends a block before tile 1, and its output is
+            // stored while tile 1 works on its diagonal block
+            if (j == n0 - 1 && leader) mma_commit(&bars->o_full[0]);
           }
           const uint32_t gk = gj + 1;
           const int ks = gk & 1;
@@ -347,10 +352,12 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             tc_fence_after();
             if (j + 1 < n0) { qk(0, ks); if (leader) mma_commit(&bars->s_full[0]); }
           }
+          if (j == 0 && !mbar_wait(&bars->o_empty[1], (ui & 1) ^ 1u, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
           if (!mbar_wait(&bars->p_full[1], gs1 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
           tc_fence_after();
           pv(1, vs, j > 0);
           ++gs1;
+          if (j == n - 1 && leader) mma_commit(&bars->o_full[1]);
           if (leader) mma_commit(&bars->v_empty[vs]);
           if (j + 1 < n) {
             qk(1, ks);
@@ -360,7 +367,6 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           }
         }
         if (!ok) break;
-        if (leader) mma_commit(&bars->o_full);
         g += n;
       }
       if (issued) {
@@ -487,7 +493,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[t]);
     }
-    if (!ok || !mbar_wait(&bars->o_full, ui & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
+    if (!ok || !mbar_wait(&bars->o_full[t], ui & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_MMA)) {
       ok = false;
       break;
     }
@@ -524,7 +530,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           // every TMEM read of O is done: the next unit's first P.V may overwrite it
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->o_empty);
+          if (lane == 0) mbar_arrive(&bars->o_empty[t]);
         }
         fence_proxy_async_smem();
         __syncwarp();
