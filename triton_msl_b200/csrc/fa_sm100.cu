@@ -457,11 +457,13 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         m_run = m_new;
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      // p = 2^(s*scale_log2 - m). The MUFU ex2 costs 8 cycles per warp
-      // instruction per SM sub-partition (measured on B200); with two tiles per
-      // sub-partition that alone would equal the tensor core's time per key
-      // block, so every other key pair uses exp2_poly2 on the FMA pipe
-      // (measured best among 0, 1/8, 1/4, 3/8, 1/2 and 5/8 of the pairs).
+      // p = 2^(s*scale_log2 - m). Measured on B200, per warp instruction per SM
+      // sub-partition: MUFU ex2 8 cycles on its own pipe; f32x2 FMA/ADD 2 issue
+      // cycles (no gain over two scalar ops), max / cvt 2 on the ALU pipe. All
+      // exponentials on the MUFU would take as long as the tensor core's work
+      // per key block; the FMA-pipe cubic costs ~9 issue slots per score. Share
+      // on the MUFU measured best: 5/8 of the key pairs at D=128, 1/2 (every
+      // other pair) at D <= 64.
       const f2_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_use, -m_use);
       f2_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t p[kBN / 2];
@@ -470,7 +472,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const f2_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
         float x0, x1, p0, p1;
         f2_unpack(x2, x0, x1);
-        if ((i & 1) == 0) {
+        if (D == 128 ? ((i & 7) < 5) : ((i & 1) == 0)) {
           p0 = ex2(x0);
           p1 = ex2(x1);
         } else {
