@@ -65,3 +65,15 @@ def test_workspace_query():
     assert L.b2_query_workspace(1, 0, 65536, 4096, 0) == 0       # softmax: none
     assert L.b2_query_workspace(1, 3, 1, 1 << 24, 0) > 0         # 1 x 16M sum: split path
     assert L.b2_query_workspace(0, 8192, 8192, 8192, 1) == 0
+
+
+def test_fa_host_pipeline_rejects_bad_inputs():
+    import torch
+    import triton_msl_b200 as b2
+    q = torch.zeros(1, 2, 8, 32, dtype=torch.float16)
+    with pytest.raises(ValueError):
+        b2.flash_attn_fwd_host(q, q, q[:, :1])
+    with pytest.raises(ValueError):
+        b2.flash_attn_fwd_host(q.transpose(1, 2), q, q)
+    with pytest.raises(TypeError):
+        b2.flash_attn_fwd_host(q, q.float(), q)

@@ -433,3 +433,17 @@ def test_gemm_softmax_epilogue_fp32_and_limits():
     _check(c, O.ref_gemm(a, b, None, "softmax"), torch.float32)
     with pytest.raises(b2.B2Unsupported):
         b2.gemm(a.to(DEV), _rand((64, 300), torch.float32, 76).to(DEV), None, "softmax")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("chunks", [1, 3, 64])
+def test_fa_host_pipeline_matches_device_path(causal, chunks):
+    """flash_attn_fwd_host (host tensors, copies overlapped with the kernel per
+    (batch, head) chunk) returns exactly what the device entry point returns."""
+    q, k, v = (_rand((2, 5, 300, 64), torch.float16, s, 0.5).pin_memory() for s in (91, 92, 93))
+    o = b2.flash_attn_fwd_host(q, k, v, causal=causal, chunks=chunks)
+    torch.cuda.synchronize()
+    assert not o.is_cuda
+    ref = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal).cpu()
+    assert torch.equal(o, ref)
+    _check(o, O.ref_attention(q, k, v, causal), torch.float16)

@@ -10,6 +10,7 @@ from .ops import (  # noqa: F401
     flash_attn_fwd, gemm, row_softmax, row_layernorm, row_rmsnorm, row_sum, row_max,
     row_min, row_argmax, row_argmin,
 )
+from .host_pipeline import flash_attn_fwd_host  # noqa: F401
 
 from . import compile_backend as _cb
 

@@ -1,0 +1,109 @@
+"""Attention over host-resident tensors with copies and compute overlapped.
+
+``flash_attn_fwd_host(q, k, v, causal, sm_scale)`` takes q/k/v [B, H, S, D] in
+(pinned) host memory and returns o in pinned host memory. The (batch, head)
+slices are independent, so the call splits them into chunks and runs three
+CUDA streams: host->device copies of chunk c+1 and device->host copies of
+chunk c-1 proceed while the tensor-core kernel works on chunk c. The two copy
+directions use separate copy engines, so a call costs about the host->device
+transfer of q, k and v plus one chunk's kernel and read-back, instead of the
+sum of all three phases.
+
+This is the path a caller whose tensors live in host memory uses (the
+reference hands host buffers to its kernels the same way, driver.py:692+);
+``flash_attn_fwd`` remains the device-tensor entry point.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import ops
+
+_STREAMS: Dict[int, Tuple[torch.cuda.Stream, torch.cuda.Stream, torch.cuda.Stream]] = {}
+
+
+def _streams(dev: torch.device):
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    s = _STREAMS.get(idx)
+    if s is None:
+        with torch.cuda.device(idx):
+            s = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
+        _STREAMS[idx] = s
+    return s
+
+
+def flash_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                        sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                        chunks: int = 4, device: Optional[torch.device] = None) -> torch.Tensor:
+    """o = softmax(sm_scale * q @ k^T [causal]) @ v for host tensors [B, H, S, D].
+
+    q, k, v: CPU tensors of one shape and dtype, contiguous (pinned memory makes
+    the copies asynchronous; pageable memory works but serialises them).
+    out: optional contiguous CPU tensor like q (pinned), else one is allocated.
+    chunks: number of (batch, head) groups pipelined through the GPU.
+    The returned tensor is complete when the current CUDA stream of `device`
+    reaches this point (synchronise it, or an event recorded on it, before
+    reading).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.is_cuda:
+            raise ValueError(f"flash_attn_fwd_host: {name} must be a host tensor "
+                             "(use flash_attn_fwd for device tensors)")
+        if not t.is_contiguous():
+            raise ValueError(f"flash_attn_fwd_host: {name} must be contiguous")
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("flash_attn_fwd_host: q, k, v must all be [B, H, S, D] of one shape")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError("flash_attn_fwd_host: q, k, v must share a dtype")
+    B, H, S, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.is_cuda or not out.is_contiguous():
+        raise ValueError("flash_attn_fwd_host: out must be a contiguous host tensor like q")
+    BH = B * H
+    if BH == 0 or S == 0:
+        return out
+    qf, kf, vf, of = (t.view(BH, S, D) for t in (q, k, v, out))
+    s_in, s_comp, s_out = _streams(dev)
+    cur = torch.cuda.current_stream(dev)
+    n = max(1, min(int(chunks), BH))
+    bounds = [(BH * c) // n for c in range(n + 1)]
+    with torch.cuda.device(dev):
+        # the copies may not start before earlier work on the caller's stream
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        dq, dk, dv = (torch.empty((BH, S, D), dtype=q.dtype, device=dev) for _ in range(3))
+        for t in (dq, dk, dv):
+            t.record_stream(s_in)
+            t.record_stream(s_comp)
+        last = None
+        for c in range(n):
+            h0, h1 = bounds[c], bounds[c + 1]
+            if h1 == h0:
+                continue
+            with torch.cuda.stream(s_in):
+                for dst, src in ((dq, qf), (dk, kf), (dv, vf)):
+                    dst[h0:h1].copy_(src[h0:h1], non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            s_comp.wait_event(ev_in)
+            with torch.cuda.stream(s_comp):
+                o = ops.flash_attn_fwd(dq[h0:h1].unsqueeze(0), dk[h0:h1].unsqueeze(0),
+                                       dv[h0:h1].unsqueeze(0), causal, sm_scale)
+                ev_c = torch.cuda.Event()
+                ev_c.record(s_comp)
+            o.record_stream(s_out)
+            s_out.wait_event(ev_c)
+            with torch.cuda.stream(s_out):
+                of[h0:h1].copy_(o[0], non_blocking=True)
+                last = torch.cuda.Event()
+                last.record(s_out)
+        if last is not None:
+            cur.wait_event(last)
+    return out
