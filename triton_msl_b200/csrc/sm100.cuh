@@ -116,13 +116,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, uint64_t
       "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
-// Prefetch one tile of a tensor map into L2 (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_l2_4d(const void* map, int x, int y, int z, int w) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map),
-               "r"(x), "r"(y), "r"(z), "r"(w)
-               : "memory");
-}
-
 // TMA tile store shared -> global (bulk-group completion), and the group waits.
 __device__ __forceinline__ void tma_store_2d(const void* src, const void* map, int x, int y) {
   asm volatile(
