@@ -458,8 +458,9 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
       // p = 2^(s*scale_log2 - m). Measured on B200, per warp instruction per SM
-      // sub-partition: MUFU ex2 8 cycles on its own pipe; f32x2 FMA/ADD 2 issue
-      // cycles (no gain over two scalar ops), max / cvt 2 on the ALU pipe. All
+      // sub-partition: MUFU ex2 8 cycles on its own pipe; f32x2 FMA/ADD 2 cycles
+      // (yet a scalar-FFMA version of this loop measured 10 % slower), max / cvt
+      // 2 on the ALU pipe. All
       // exponentials on the MUFU would take as long as the tensor core's work
       // per key block; the FMA-pipe cubic costs ~9 issue slots per score. Share
       // on the MUFU measured best: 5/8 of the key pairs at D=128, 1/2 (every
