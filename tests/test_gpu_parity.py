@@ -447,3 +447,27 @@ def test_fa_host_pipeline_matches_device_path(causal, chunks):
     ref = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal).cpu()
     assert torch.equal(o, ref)
     _check(o, O.ref_attention(q, k, v, causal), torch.float16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fa_many_units_per_cta_and_rescales(dtype, D, causal):
+    """More (query block, head) units than SMs, so each persistent CTA runs several
+    units of different lengths back to back (per-tile O / Q hand-over between
+    units), with scores spread wide enough (x3 inputs) that the running max grows
+    by more than 2^8 mid-row and the O rescale path runs."""
+    q, k, v = (_rand((4, 50, 384, D), dtype, s, 1.5) for s in (94, 95, 96))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    assert b2.last_kernel() == "fa_sm100"
+    _check(o, O.ref_attention(q, k, v, causal), dtype)
+    assert b2.device_status(0) == 0
+
+
+@pytest.mark.parametrize("S", [1, 2, 8])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fa_tiny_sequences(S, causal):
+    q, k, v = (_rand((3, 4, S, 128), torch.float16, s, 0.5) for s in (97, 98, 99))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    assert b2.last_kernel() == "fa_sm100"
+    _check(o, O.ref_attention(q, k, v, causal), torch.float16)
