@@ -471,3 +471,19 @@ def test_fa_tiny_sequences(S, causal):
     o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
     assert b2.last_kernel() == "fa_sm100"
     _check(o, O.ref_attention(q, k, v, causal), torch.float16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fa_rescale_when_later_keys_dominate(dtype, causal):
+    """Keys of later blocks score far higher than the first block's, so the
+    running max grows by more than 2^8 after the first block and O (and l) are
+    rescaled mid-row."""
+    q = _rand((2, 3, 640, 128), torch.float32, 101, 1.0)
+    k = _rand((2, 3, 640, 128), torch.float32, 102, 1.0)
+    k[:, :, 256:] *= 5.0
+    v = _rand((2, 3, 640, 128), torch.float32, 103, 1.0)
+    q, k, v = (t.to(dtype) for t in (q, k, v))
+    o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    assert b2.last_kernel() == "fa_sm100"
+    _check(o, O.ref_attention(q, k, v, causal), dtype)
