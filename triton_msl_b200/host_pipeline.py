@@ -83,16 +83,22 @@ def flash_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
             t.record_stream(s_in)
             t.record_stream(s_comp)
         last = None
+        # All host->device copies are queued first, so the copy engine never waits
+        # for the host to issue the next chunk's copies.
+        ev_in = []
+        with torch.cuda.stream(s_in):
+            for c in range(n):
+                h0, h1 = bounds[c], bounds[c + 1]
+                for dst, src in ((dq, qf), (dk, kf), (dv, vf)):
+                    dst[h0:h1].copy_(src[h0:h1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+                ev_in.append(ev)
         for c in range(n):
             h0, h1 = bounds[c], bounds[c + 1]
             if h1 == h0:
                 continue
-            with torch.cuda.stream(s_in):
-                for dst, src in ((dq, qf), (dk, kf), (dv, vf)):
-                    dst[h0:h1].copy_(src[h0:h1], non_blocking=True)
-                ev_in = torch.cuda.Event()
-                ev_in.record(s_in)
-            s_comp.wait_event(ev_in)
+            s_comp.wait_event(ev_in[c])
             with torch.cuda.stream(s_comp):
                 o = ops.flash_attn_fwd(dq[h0:h1].unsqueeze(0), dk[h0:h1].unsqueeze(0),
                                        dv[h0:h1].unsqueeze(0), causal, sm_scale)
