@@ -450,7 +450,7 @@ def test_fa_host_pipeline_matches_device_path(causal, chunks):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [32, 64, 128])
 @pytest.mark.parametrize("causal", [False, True])
 def test_fa_many_units_per_cta_and_rescales(dtype, D, causal):
     """More (query block, head) units than SMs, so each persistent CTA runs several
@@ -464,25 +464,28 @@ def test_fa_many_units_per_cta_and_rescales(dtype, D, causal):
     assert b2.device_status(0) == 0
 
 
+@pytest.mark.parametrize("D", [32, 128])
 @pytest.mark.parametrize("S", [1, 2, 8])
 @pytest.mark.parametrize("causal", [False, True])
-def test_fa_tiny_sequences(S, causal):
-    q, k, v = (_rand((3, 4, S, 128), torch.float16, s, 0.5) for s in (97, 98, 99))
+def test_fa_tiny_sequences(S, causal, D):
+    q, k, v = (_rand((3, 4, S, D), torch.float16, s, 0.5) for s in (97, 98, 99))
     o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
     assert b2.last_kernel() == "fa_sm100"
     _check(o, O.ref_attention(q, k, v, causal), torch.float16)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128])
 @pytest.mark.parametrize("causal", [False, True])
-def test_fa_rescale_when_later_keys_dominate(dtype, causal):
+def test_fa_rescale_when_later_keys_dominate(dtype, D, causal):
     """Keys of later blocks score far higher than the first block's, so the
     running max grows by more than 2^8 after the first block and O (and l) are
-    rescaled mid-row."""
-    q = _rand((2, 3, 640, 128), torch.float32, 101, 1.0)
-    k = _rand((2, 3, 640, 128), torch.float32, 102, 1.0)
+    rescaled mid-row. For D <= 64 l is accumulated by the tensor core beside O,
+    so this also checks its rescale."""
+    q = _rand((2, 3, 640, D), torch.float32, 101, 1.0)
+    k = _rand((2, 3, 640, D), torch.float32, 102, 1.0)
     k[:, :, 256:] *= 5.0
-    v = _rand((2, 3, 640, 128), torch.float32, 103, 1.0)
+    v = _rand((2, 3, 640, D), torch.float32, 103, 1.0)
     q, k, v = (t.to(dtype) for t in (q, k, v))
     o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
     assert b2.last_kernel() == "fa_sm100"

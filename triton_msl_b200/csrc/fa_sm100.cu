@@ -23,6 +23,11 @@
 // earlier MMAs), which is what lets the softmax warps rescale O_t safely.
 // O is only rescaled when a row max grows by more than 2^8 (the stale max is
 // used consistently for P and l, so the result is exact up to rounding).
+// For D <= 64, where TMEM has columns to spare, the row sums l come from the
+// tensor core too: after each P_t.V an N=16 MMA of P_t with a ones tile
+// accumulates l_t into 16 TMEM columns L_t beside O (every column holds the
+// row sum), so the softmax warps issue no per-score additions; L_t is
+// rescaled with O_t and read once per unit.
 #include "sm100.cuh"
 
 namespace b2 {
@@ -70,8 +75,26 @@ struct FaCfg {
   static constexpr uint32_t kSBO = 8 * kAtomBytes;          // 8-row group pitch
   // output staging: per softmax warp one 32-row x atom-wide block
   static constexpr uint32_t kOutStageBytes = 32 * kAtomBytes;
-  static constexpr size_t kSmem = 1024 + 6 * kTileBytes + 8 * kOutStageBytes + sizeof(FaBarriers);
+  // row sums on the tensor core (TMEM: 2 x (128 + D + 16) columns <= 512)
+  static constexpr bool kSumMma = D <= 64;
+  static constexpr uint32_t kOnesBytes = kSumMma ? 1024 : 0;  // ones tile, B of the l MMA
+  static constexpr size_t kSmem =
+      1024 + 6 * kTileBytes + 8 * kOutStageBytes + kOnesBytes + sizeof(FaBarriers);
 };
+
+// Of every 8 key pairs, how many take their exponentials on the MUFU (the
+// rest use exp2_poly2 on the FMA pipe).
+#ifndef B2_FA_MUFU8_D128
+#define B2_FA_MUFU8_D128 5
+#endif
+#ifndef B2_FA_MUFU8_SMALL
+#define B2_FA_MUFU8_SMALL 4
+#endif
+template <int D>
+__device__ __forceinline__ constexpr bool on_mufu(int i) {
+  return D == 128 ? ((i & 7) < B2_FA_MUFU8_D128)
+                  : (B2_FA_MUFU8_SMALL == 4 ? ((i & 1) == 0) : ((i & 7) < B2_FA_MUFU8_SMALL));
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -151,7 +174,8 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   uint8_t* sK = smem + 2 * Cfg::kTileBytes;        // 2 stages
   uint8_t* sV = smem + 4 * Cfg::kTileBytes;        // 2 stages
   uint8_t* sO = smem + 6 * Cfg::kTileBytes;        // output staging, 8 warps
-  FaBarriers* bars = reinterpret_cast<FaBarriers*>(sO + 8 * Cfg::kOutStageBytes);
+  uint8_t* sOnes = sO + 8 * Cfg::kOutStageBytes;  // kOnesBytes of 1.0 (D <= 64)
+  FaBarriers* bars = reinterpret_cast<FaBarriers*>(sOnes + Cfg::kOnesBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_units = num_qblk * BH;
@@ -208,12 +232,22 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  if constexpr (Cfg::kSumMma) {
+    // 1.0 in every element (fp16 0x3C00, bf16 0x3F80); the tensor core reads
+    // the tile through the async proxy.
+    if (threadIdx.x < Cfg::kOnesBytes / 16) {
+      const uint32_t w = BF16 ? 0x3F803F80u : 0x3C003C00u;
+      reinterpret_cast<uint4*>(sOnes)[threadIdx.x] = make_uint4(w, w, w, w);
+      fence_proxy_async_smem();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO[2] = {tmem + 256, tmem + 256 + D};
+  const uint32_t tL[2] = {tmem + 256 + 2 * D, tmem + 256 + 2 * D + 16};  // D <= 64 only
 
   // Each role branch executes its own setmaxnreg, so the compiler sees one
   // register budget per region.
@@ -307,6 +341,20 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (leader) mma_f16_ts(d, pa + k * 8, db + ((k * 16 * Cfg::kAtomBytes) >> 4), idO, k > 0 ? 1u : acc0);
         }
       };
+      // l_t += P_t . ones (D <= 64): one K=16 slice of the ones tile serves
+      // every key step, since all its elements are equal. No swizzle; the
+      // K-major core matrices lie within the tile's first 512 bytes.
+      constexpr uint32_t idL = idesc_f16(kBM, 16, BF16, false, false);
+      const uint64_t dones = sdesc(smem_addr(sOnes), 128, 256, 0);
+      auto pl = [&](int t, bool accumulate) {
+        if constexpr (Cfg::kSumMma) {
+          const uint32_t pa = t ? tS[1] : tS[0];
+#pragma unroll
+          for (int k = 0; k < kBN / 16; ++k)
+            if (leader) mma_f16_ts(tL[t], pa + k * 8, dones, idL, (k > 0 || accumulate) ? 1u : 0u);
+        }
+      };
+      (void)dones;
       uint32_t g = 0;             // K/V ring position
       uint32_t gs0 = 0, gs1 = 0;  // P blocks consumed per tile (p_full parity)
       uint32_t ui = 0;
@@ -340,6 +388,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             if (!mbar_wait(&bars->p_full[0], gs0 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
             tc_fence_after();
             pv(0, vs, j > 0);
+            pl(0, j > 0);
             ++gs0;
             // causal: tile 0 ends a block before tile 1, and its output is
             // stored while tile 1 works on its diagonal block
@@ -356,6 +405,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           if (!mbar_wait(&bars->p_full[1], gs1 & 1, abort_flag, &g_fa_status, DEV_TIMEOUT_EPI)) { ok = false; break; }
           tc_fence_after();
           pv(1, vs, j > 0);
+          pl(1, j > 0);
           ++gs1;
           if (j == n - 1 && leader) mma_commit(&bars->o_full[1]);
           if (leader) mma_commit(&bars->v_empty[vs]);
@@ -473,23 +523,21 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const f2_t x2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
         float x0, x1, p0, p1;
         f2_unpack(x2, x0, x1);
-        if (D == 128 ? ((i & 7) < 5) : ((i & 1) == 0)) {
+        if (on_mufu<D>(i)) {
           p0 = ex2(x0);
           p1 = ex2(x1);
         } else {
           exp2_poly2(x0, x1, p0, p1);
         }
-        acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(p0, p1));
+        if constexpr (!Cfg::kSumMma) acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(p0, p1));
         p[i] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
       }
-      float rowsum;
-      {
+      if constexpr (!Cfg::kSumMma) {
         const f2_t a01 = f2_add(acc2[0], acc2[1]), a23 = f2_add(acc2[2], acc2[3]);
         float u0, u1;
         f2_unpack(f2_add(a01, a23), u0, u1);
-        rowsum = u0 + u1;
+        l_run = l_run * alpha + (u0 + u1);
       }
-      l_run = l_run * alpha + rowsum;
 #pragma unroll
       for (int c = 0; c < kBN / 2 / 32; ++c) {
         uint32_t r[32];
@@ -507,6 +555,11 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           tmem_st32(tO[t] + lane_off + c * 32, r);
         }
+        if constexpr (Cfg::kSumMma) {
+          const uint32_t lc = tmem_ld1(tL[t] + lane_off);
+          tmem_ld_wait();
+          tmem_st1(tL[t] + lane_off, __float_as_uint(__uint_as_float(lc) * alpha));
+        }
       }
       tmem_st_wait();
       tc_fence_before();
@@ -519,6 +572,10 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
     {
       tc_fence_after();
+      if constexpr (Cfg::kSumMma) {
+        l_run = __uint_as_float(tmem_ld1(tL[t] + lane_off));
+        tmem_ld_wait();
+      }
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       // O rows -> swizzled staging (one atom-wide 32-row block per warp) -> TMA
       // store; rows >= S are clipped by the TMA unit. One atom at a time.
