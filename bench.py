@@ -72,24 +72,44 @@ class ClockSampler:
         self._t = None
 
     def _run(self):
-        while not self._stop.is_set():
-            try:
-                r = subprocess.run(["nvidia-smi", "-i", str(self.gpu),
-                                    f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                                   capture_output=True, text=True, timeout=5)
-                if r.returncode == 0 and r.stdout.strip():
-                    self.samples.append([s.strip() for s in r.stdout.strip().split(",")])
-            except Exception:
-                return
-            self._stop.wait(0.2)
+        # One long-running `nvidia-smi -lms 200`: the driver query is set up once,
+        # not once per sample (a fresh nvidia-smi per sample perturbed the timed
+        # launches).
+        try:
+            self._p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self._first.set()
+            return
+        for line in self._p.stdout:
+            if line.strip():
+                self.samples.append([f.strip() for f in line.strip().split(",")])
+                self._first.set()
+            if self._stop.is_set():
+                break
+        self._first.set()
+
+    def wait_first(self, timeout: float) -> None:
+        """Block until the first sample arrived (or timeout): the query process is up."""
+        self._first.wait(timeout)
 
     def __enter__(self):
+        self._p = None
+        self._first = threading.Event()
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
         return self
 
     def __exit__(self, *a):
         self._stop.set()
+        if self._p is not None:
+            self._p.terminate()
+            try:
+                self._p.wait(timeout=5)
+            except Exception:
+                self._p.kill()
         if self._t:
             self._t.join(timeout=10)
 
@@ -140,12 +160,19 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 def time_launches(fn, steps, warmup, flush_buf, world):
-    """Device time per launch (ms): events around each launch, L2 flushed between."""
-    for _ in range(warmup):
-        fn()
+    """Device time per launch (ms): events around each launch, L2 flushed between.
+
+    The warm-up steps (flush + launch, like the timed ones) are queued after the
+    opening synchronize + barrier and run straight into the timed steps, outside
+    every event pair, which also puts the host ahead of the device, so no step's
+    events include host launch latency.
+    """
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    for _ in range(warmup):  # the same sequence as a timed step
+        flush_buf.zero_()
+        fn()
     evs = []
     st = torch.cuda.current_stream()
     for _ in range(steps):
@@ -240,16 +267,23 @@ def run_b2(args, world, rank, local):
     kern = b2.last_kernel()
     if kern != "fa_sm100":
         raise RuntimeError(f"headline FA ran on {kern}, not the tensor-core kernel")
-    # Bring the GPU out of idle clocks before the W warm-up steps: ~0.3 s of the
-    # same launches, untimed (the first timed steps otherwise catch the ramp).
-    t_end = time.time() + 0.3
-    while time.time() < t_end:
-        for _ in range(20):
-            fa()
-        torch.cuda.synchronize()
+    # Clock sampling starts first, so that the sampler's own start-up is over
+    # before anything is timed; its samples cover the pre-warm and the timed
+    # region, both running this kernel back to back.
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.__enter__()
+    # Bring the GPU out of idle clocks before the W warm-up steps: at least 0.3 s
+    # of the same launches, untimed (the first timed steps otherwise catch the
+    # ramp), and until the clock sampler is running (at most 5 s).
+    t0 = time.time()
+    while True:
+        for _ in range(20):
+            fa()
+        torch.cuda.synchronize()
+        el = time.time() - t0
+        if el >= 5.0 or (el >= 0.3 and (sampler is None or sampler._first.is_set())):
+            break
     try:
         times = time_launches(fa, args.steps, args.warmup, flush, world)
     finally:
