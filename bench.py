@@ -267,23 +267,15 @@ def run_b2(args, world, rank, local):
     kern = b2.last_kernel()
     if kern != "fa_sm100":
         raise RuntimeError(f"headline FA ran on {kern}, not the tensor-core kernel")
-    # Clock sampling starts first, so that the sampler's own start-up is over
-    # before anything is timed; its samples cover the pre-warm and the timed
-    # region, both running this kernel back to back.
+    # Clock sampling starts first and the sampler's start-up is over (first sample
+    # in, at most 5 s) before anything is timed. No extended pre-warm: on these
+    # parts the idle SM clock is already the maximum, and a sub-second loop of
+    # back-to-back launches before the timed steps tripped the power cap
+    # (clocks down to ~1590 MHz for the timed steps that followed).
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.__enter__()
-    # Bring the GPU out of idle clocks before the W warm-up steps: at least 0.3 s
-    # of the same launches, untimed (the first timed steps otherwise catch the
-    # ramp), and until the clock sampler is running (at most 5 s).
-    t0 = time.time()
-    while True:
-        for _ in range(20):
-            fa()
-        torch.cuda.synchronize()
-        el = time.time() - t0
-        if el >= 5.0 or (el >= 0.3 and (sampler is None or sampler._first.is_set())):
-            break
+        sampler.wait_first(5.0)
     try:
         times = time_launches(fa, args.steps, args.warmup, flush, world)
     finally:
