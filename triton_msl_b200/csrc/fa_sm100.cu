@@ -80,6 +80,9 @@ struct FaCfg {
   static constexpr uint32_t kOnesBytes = kSumMma ? 1024 : 0;  // ones tile, B of the l MMA
   static constexpr size_t kSmem =
       1024 + 6 * kTileBytes + 8 * kOutStageBytes + kOnesBytes + sizeof(FaBarriers);
+  // TMEM: S0 | S1 (128 columns each) | O0 | O1 (D each) | L0 | L1 (16 each, D <= 64)
+  static_assert(2 * (kBN + D + (kSumMma ? 16 : 0)) <= (int)kTmemCols, "TMEM columns exceeded");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA exceeded");
 };
 
 // Of every 8 key pairs, how many take their exponentials on the MUFU (the
