@@ -158,7 +158,12 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out,
  *    rows * ceil(cols / 65536) <= 16384 partial results; larger requests fail
  *    with B2_EINVAL (use b2_row_op with a workspace for those).
  *  - The first call on a device looks up the array's device address with that
- *    device current; make that first call before any stream capture.
+ *    device current; make that first call before any stream capture. A
+ *    successful lookup is kept for the life of the process (so a
+ *    cudaDeviceReset, or a non-primary driver context made current, is not
+ *    supported afterwards); a failed one returns B2_ELAUNCH and is retried by
+ *    the next call.
+ *  - `stream` must belong to the current device (B2_EINVAL otherwise).
  *  - All calls share the one array: calls whose kernels overlap on the GPU
  *    (different streams, or different host threads, same device) race.
  *    Every scratch slot a call reads is written by the same call first, so
@@ -177,6 +182,27 @@ size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t 
 /* OR of the device status bits written by bounded waits on `device` since the
  * last clear (0 = no wait expired). Synchronises that device. clear != 0 resets it. */
 int b2_device_status(int device, int clear, uint32_t* status_out);
+
+/* Device status bits (b2_device_status). */
+#define B2_STATUS_TIMEOUT_TMA 0x1u  /* a consumer gave up waiting for a TMA fill */
+#define B2_STATUS_TIMEOUT_MMA 0x2u  /* a waiter gave up on a tensor-core commit */
+#define B2_STATUS_TIMEOUT_EPI 0x4u  /* a waiter gave up on the epilogue / softmax warps */
+#define B2_STATUS_TIMEOUT_SLOT 0x8u /* the TMA producer gave up waiting for a free stage */
+
+/*
+ * Failure-path test of the bounded device waits (no counterpart in the
+ * reference; its fast-path failure contract is "return False and take the
+ * generic path", triton_msl/autotuning/_fast_matmul_dispatch.py:152-158).
+ * Launches the tensor-core GEMM on fp16 A[M,K] (row-major) and B given as
+ * [N,K] (row-major), C fp16 [M,N], with its TMA producer told to load
+ * nothing and every wait limited to wait_limit_ns (<= 1 s). The MMA warp's
+ * wait for the first operand stage runs out, the CTA abort flag stops the
+ * other roles, TMEM is freed and the kernel returns; C is left unwritten.
+ * A later b2_device_status() then reports B2_ETIMEOUT with
+ * B2_STATUS_TIMEOUT_TMA set. Returns the launch status (B2_OK when queued).
+ */
+int b2_test_stalled_gemm(const void* A, const void* Bm, void* C, int64_t M, int64_t N, int64_t K,
+                         uint64_t wait_limit_ns, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -19,6 +19,7 @@ LIB_PATH = Path(os.environ.get("B2MSL_LIBRARY", PKG / "libb2msl.so"))
 
 B2_OK, B2_EINVAL, B2_EUNSUPPORTED, B2_ELAUNCH, B2_ETIMEOUT = 0, -1, -2, -3, -4
 B2_F32, B2_F16, B2_BF16, B2_I64 = 0, 1, 2, 3
+STATUS_TIMEOUT_TMA, STATUS_TIMEOUT_MMA, STATUS_TIMEOUT_EPI, STATUS_TIMEOUT_SLOT = 1, 2, 4, 8
 ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4, "softmax": 5}
 ROW_OPS = {"softmax": 0, "layernorm": 1, "rmsnorm": 2, "sum": 3, "max": 4,
            "argmax": 5, "min": 6, "argmin": 7}
@@ -39,6 +40,8 @@ SIGNATURES = {
                      ctypes.c_void_p]),
     "b2_row_reduce_noalloc": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
                               + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p]),
+    "b2_test_stalled_gemm": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 3
+                             + [ctypes.c_uint64, ctypes.c_void_p]),
     "b2_query_workspace": (ctypes.c_size_t, [ctypes.c_int] + [ctypes.c_int64] * 4),
     "b2_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_uint32)]),

@@ -18,8 +18,13 @@ Dynamo captures and replaced by calls to the custom ops:
   over the last dim, ``sum / amax / amin / argmax / argmin(dim=-1)`` -> row ops
 
 A node is rewritten only when its traced example value says the replacement
-is exact: CUDA tensors, float32/float16/bfloat16, shapes the ops accept. The
-rest of the graph runs as captured (``inner="eager"``) or through Inductor
+is exact: CUDA tensors, float32/float16/bfloat16, shapes the ops accept, and
+no autograd history needed. The ops are forward-only (the reference's
+templates are forward kernels too), so a node whose output requires grad --
+a training graph -- is left to PyTorch and backward stays correct; compile
+under ``torch.no_grad()`` / ``torch.inference_mode()`` (or with parameters
+that do not require grad) to route the patterns. The rest of the graph runs
+as captured (``inner="eager"``) or through Inductor
 (``inner="inductor"``).
 """
 from __future__ import annotations
@@ -118,6 +123,60 @@ def _sdpa(q, k, v, causal, scale):
     return b2ops.flash_attn_fwd(q, k, v, causal=causal, sm_scale=scale)
 
 
+def _mha_core(x_q, x_k, x_v, num_heads, w_in, b_in, w_out, b_out, causal, batch_first):
+    """Multi-head attention with packed input projection through the b2msl ops:
+    in-projection GEMMs, the heads as strided [B, H, S, Dh] views into the
+    projection output (the attention kernel takes any strides), attention,
+    out-projection GEMM. Inputs are [B, S, E] when batch_first else [S, B, E]."""
+    if not batch_first:
+        x_q, x_k, x_v = (t.transpose(0, 1) for t in (x_q, x_k, x_v))
+    B, S, E = x_q.shape
+    Dh = E // num_heads
+    if x_q is x_k and x_k is x_v:
+        qkv = _linear_act(x_q, w_in, b_in, "none").view(B, S, 3, num_heads, Dh)
+        q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+    else:
+        ws = w_in.chunk(3)
+        bs = b_in.chunk(3) if b_in is not None else (None, None, None)
+        q, k, v = (_linear_act(t, w_, b_, "none").view(B, t.shape[1], num_heads, Dh).transpose(1, 2)
+                   for t, w_, b_ in zip((x_q, x_k, x_v), ws, bs))
+    o = b2ops.flash_attn_fwd(q, k, v, causal=causal, sm_scale=Dh ** -0.5)
+    o = o.transpose(1, 2).reshape(B, S, E)
+    y = _linear_act(o, w_out, b_out, "none")
+    return y if batch_first else y.transpose(0, 1)
+
+
+def _mha_functional(q, k, v, num_heads, w_in, b_in, w_out, b_out, causal):
+    """F.multi_head_attention_forward (sequence-first inputs) -> (out, None)."""
+    return _mha_core(q, k, v, num_heads, w_in, b_in, w_out, b_out, causal, False), None
+
+
+def _mha_native(q, k, v, num_heads, w_in, b_in, w_out, b_out):
+    """torch._native_multi_head_attention (batch-first inputs) -> (out, None)."""
+    return _mha_core(q, k, v, num_heads, w_in, b_in, w_out, b_out, False, True), None
+
+
+def _encoder_layer(x, num_heads, w_in, b_in, w_out, b_out, use_gelu, norm_first, eps,
+                   n1w, n1b, n2w, n2b, l1w, l1b, l2w, l2b):
+    """The inference fast path of nn.TransformerEncoderLayer
+    (torch._transformer_encoder_layer_fwd, batch-first, no mask) through the
+    b2msl ops: self-attention, LayerNorms and the feed-forward GEMMs with the
+    activation fused into the first."""
+    act = "gelu" if use_gelu else "relu"
+
+    def ff(t):
+        return _linear_act(_linear_act(t, l1w, l1b, act), l2w, l2b, "none")
+
+    def sa(t):
+        return _mha_core(t, t, t, num_heads, w_in, b_in, w_out, b_out, False, True)
+
+    if norm_first:
+        x = x + sa(b2ops.row_layernorm(x, n1w, n1b, eps))
+        return x + ff(b2ops.row_layernorm(x, n2w, n2b, eps))
+    x = b2ops.row_layernorm(x + sa(x), n1w, n1b, eps)
+    return b2ops.row_layernorm(x + ff(x), n2w, n2b, eps)
+
+
 def _rowred(x, kind):
     return getattr(b2ops, f"row_{kind}")(x)
 
@@ -153,9 +212,11 @@ class Rewriter:
         if len(users) != 1:
             return None, None
         u = users[0]
-        if u.op in ("call_function", "call_method") and _in(u, _ACTS) and len(u.args) == 1 and not u.kwargs:
+        kw = {k: v for k, v in u.kwargs.items() if not (k == "inplace" and v is False)}
+        if u.op in ("call_function", "call_method") and _in(u, _ACTS) and len(u.args) == 1 and \
+                (not kw or (u.target is F.gelu and kw == {"approximate": "none"})):
             return u, _ACTS[_target_key(u)]
-        if u.op == "call_function" and u.target is F.gelu and u.kwargs.get("approximate", "none") == "tanh":
+        if u.op == "call_function" and u.target is F.gelu and kw == {"approximate": "tanh"}:
             return u, "gelu_tanh"
         # matmul -> row softmax (the reference's fused matmul-softmax template),
         # when one output tile covers a row
@@ -195,6 +256,9 @@ class Rewriter:
         return self.replaced
 
     def _visit(self, node: fx.Node):
+        out = _val(node)
+        if isinstance(out, torch.Tensor) and out.requires_grad:
+            return  # forward-only ops: keep autograd's own graph for training
         t = _target_key(node)
         ac = self.allow_cpu
         # ---- attention
@@ -210,6 +274,16 @@ class Rewriter:
                         and qv.shape[-1] <= 128:
                     s = scale if scale is not None else qv.shape[-1] ** -0.5
                     self._replace(node, _sdpa, (q, k, v, bool(causal), float(s)), "attention")
+            return
+        # ---- nn.MultiheadAttention / nn.TransformerEncoderLayer inference paths
+        if t is F.multi_head_attention_forward:
+            self._visit_mha_functional(node)
+            return
+        if t is getattr(torch, "_native_multi_head_attention", None):
+            self._visit_mha_native(node)
+            return
+        if t is getattr(torch, "_transformer_encoder_layer_fwd", None):
+            self._visit_encoder_layer(node)
             return
         # ---- explicit attention chain: matmul(softmax(matmul(q, k^T) * s), v)
         if _in(node, _MATMUL) and len(node.args) == 2:
@@ -280,6 +354,75 @@ class Rewriter:
                 self._replace(node, _rowred, (x, kind), f"row_{kind}")
             return
 
+    def _attn_weights_ok(self, E, H, *ps) -> bool:
+        ac = self.allow_cpu
+        if not isinstance(E, int) or not isinstance(H, int) or H <= 0 or E % H or E // H > 128:
+            return False
+        return all(p is None or _ok_tensor(p, ac) for p in ps)
+
+    def _visit_mha_functional(self, node: fx.Node):
+        a = node.args
+        if len(a) < 13:
+            return
+        q, k, v, E, H, w_in, b_in, bias_k, bias_v, add_zero, drop, w_out, b_out = a[:13]
+        kw = node.kwargs
+        if bias_k is not None or bias_v is not None or add_zero or kw.get("need_weights", True):
+            return
+        if kw.get("training", True) and drop not in (0, 0.0):
+            return
+        if kw.get("key_padding_mask") is not None or kw.get("attn_mask") is not None:
+            return
+        if kw.get("use_separate_proj_weight", False) or kw.get("static_k") is not None \
+                or kw.get("static_v") is not None:
+            return
+        causal = bool(kw.get("is_causal", False))
+        if causal:
+            return  # is_causal without a mask is a hint only in this function
+        ac = self.allow_cpu
+        if not all(_ok_tensor(x, ac, 3) for x in (q, k, v)):
+            return
+        qv, kv, vv = _val(q), _val(k), _val(v)
+        if not (qv.shape == kv.shape == vv.shape and qv.dtype == kv.dtype == vv.dtype):
+            return
+        if not self._attn_weights_ok(E, H, w_in, b_in, w_out, b_out) or w_in is None or w_out is None:
+            return
+        self._replace(node, _mha_functional, (q, k, v, H, w_in, b_in, w_out, b_out, False), "attention(mha)")
+
+    def _visit_mha_native(self, node: fx.Node):
+        a = node.args
+        if len(a) < 9:
+            return
+        q, k, v, E, H, w_in, b_in, w_out, b_out = a[:9]
+        mask = a[9] if len(a) > 9 else node.kwargs.get("mask")
+        need_w = a[10] if len(a) > 10 else node.kwargs.get("need_weights", True)
+        if mask is not None or need_w:
+            return
+        ac = self.allow_cpu
+        if not all(_ok_tensor(x, ac, 3) for x in (q, k, v)):
+            return
+        qv, kv, vv = _val(q), _val(k), _val(v)
+        if not (qv.shape == kv.shape == vv.shape and qv.dtype == kv.dtype == vv.dtype):
+            return
+        if not self._attn_weights_ok(E, H, w_in, b_in, w_out, b_out):
+            return
+        self._replace(node, _mha_native, (q, k, v, H, w_in, b_in, w_out, b_out), "attention(mha)")
+
+    def _visit_encoder_layer(self, node: fx.Node):
+        a = node.args
+        if len(a) < 18:
+            return
+        x, E, H, w_in, b_in, w_out, b_out, use_gelu, norm_first, eps = a[:10]
+        n1w, n1b, n2w, n2b, l1w, l1b, l2w, l2b = a[10:18]
+        mask = a[18] if len(a) > 18 else node.kwargs.get("mask")
+        if mask is not None or not _ok_tensor(x, self.allow_cpu, 3):
+            return
+        if not self._attn_weights_ok(E, H, w_in, b_in, w_out, b_out, n1w, n1b, n2w, n2b,
+                                     l1w, l1b, l2w, l2b):
+            return
+        self._replace(node, _encoder_layer, (x, H, w_in, b_in, w_out, b_out, bool(use_gelu),
+                                             bool(norm_first), float(eps), n1w, n1b, n2w, n2b,
+                                             l1w, l1b, l2w, l2b), "encoder_layer")
+
     def _explicit_attention(self, out_mm: fx.Node, sm: fx.Node, v) -> bool:
         if not _is_last_dim(_arg(sm, 1, "dim"), _val(sm)):
             return False
@@ -315,13 +458,18 @@ def rewrite(gm: fx.GraphModule, allow_cpu: bool = False) -> List[str]:
     return Rewriter(gm, allow_cpu).run()
 
 
+# Tags of the patterns replaced in the most recent graph (last_rewrites) and in
+# every graph compiled since the caller last cleared it (rewrite_log; one
+# torch.compile call can produce several graphs when Dynamo breaks the graph).
 last_rewrites: List[str] = []
+rewrite_log: List[str] = []
 
 
 def b2msl_backend(gm: fx.GraphModule, example_inputs, inner: str = "eager"):
     """Dynamo backend: rewrite the hot-path patterns, then run eagerly or via Inductor."""
     global last_rewrites
     last_rewrites = rewrite(gm)
+    rewrite_log.extend(last_rewrites)
     if inner == "inductor":
         from torch._inductor.compile_fx import compile_fx
         return compile_fx(gm, example_inputs)

@@ -16,6 +16,10 @@ namespace b2 {
 void set_error(const char* fmt, ...);
 void clear_error();
 
+// Streaming-multiprocessor count of the current device, cached per device
+// ordinal behind std::call_once (safe from several host threads). 148 on B200.
+int device_sm_count();
+
 // Device status bits, OR-ed into a per-module __device__ word by kernels and
 // read back with b2_device_status().
 enum : uint32_t {

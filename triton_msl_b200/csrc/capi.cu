@@ -28,6 +28,8 @@ int gemm_tf32x3_launch(const float*, const float*, const void*, void*, long long
 size_t row_op_workspace(int, long long, long long);
 int row_op_launch(int, const void*, const void*, const void*, void*, long long, long long,
                   long long, long long, float, int, void*, size_t, cudaStream_t);
+int gemm_stall_test_launch(const void*, const void*, void*, long long, long long, long long,
+                           unsigned long long, cudaStream_t);
 uint32_t row_read_status(bool);
 uint32_t gemm_read_status(bool);
 uint32_t fa_read_status(bool);
@@ -52,6 +54,9 @@ bool device_is_sm100() {
   return g_cc_major[dev] == 10;
 }
 
+int g_sm_count[kMaxDev];
+std::once_flag g_sm_once[kMaxDev];
+
 bool valid_float_dtype(int dt) { return dt == B2_F32 || dt == B2_F16 || dt == B2_BF16; }
 }  // namespace
 
@@ -64,6 +69,17 @@ void set_error(const char* fmt, ...) {
   t_err = buf;
 }
 void clear_error() { t_err.clear(); }
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+  std::call_once(g_sm_once[dev], [dev] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  });
+  return g_sm_count[dev];
+}
 
 }  // namespace b2
 
@@ -246,6 +262,33 @@ size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t 
     case 2: return 0;
     default: return 0;
   }
+}
+
+int b2_test_stalled_gemm(const void* A, const void* Bm, void* C, int64_t M, int64_t N, int64_t K,
+                         uint64_t wait_limit_ns, void* stream) {
+  clear_error();
+  if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31) ||
+      (K * 2) % 16 != 0) {
+    set_error("b2_test_stalled_gemm: invalid shape M=%lld N=%lld K=%lld (K*2 must be a multiple of 16)",
+              (long long)M, (long long)N, (long long)K);
+    return B2_EINVAL;
+  }
+  if (!A || !Bm || !C || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(Bm)) & 15)) {
+    set_error("b2_test_stalled_gemm: null or unaligned operand");
+    return B2_EINVAL;
+  }
+  if (wait_limit_ns == 0 || wait_limit_ns > kWaitLimitNs) {
+    set_error("b2_test_stalled_gemm: wait limit must be in (0, %llu] ns", kWaitLimitNs);
+    return B2_EINVAL;
+  }
+  if (!device_is_sm100()) {
+    set_error("b2_test_stalled_gemm: needs an sm_100 device");
+    return B2_EUNSUPPORTED;
+  }
+  const int rc = gemm_stall_test_launch(A, Bm, C, M, N, K, wait_limit_ns,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  if (rc == B2_OK) t_kernel = "gemm_sm100";
+  return rc;
 }
 
 int b2_device_status(int device, int clear, uint32_t* status_out) {

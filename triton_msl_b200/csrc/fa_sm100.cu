@@ -671,9 +671,7 @@ int launch(const void* q, const void* k, const void* v, void* o, long long B, lo
   }
   const int num_qblk = (int)((S + 2 * kBM - 1) / (2 * kBM));
   const long long units = (long long)num_qblk * B * H;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
   const long long grid = units < sms ? units : sms;  // persistent: one CTA per SM
   if (units >= (1LL << 31)) {
     set_error("b2_fa_fwd: grid too large");

@@ -93,7 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int use_tma_store,
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
-                  int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok) {
+                  int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok,
+                  unsigned long long wait_ns, int stall_producer) {
   constexpr int kRing = EpiCfg<TO>::kRing;
   constexpr uint32_t kStageOutBytes = EpiCfg<TO>::kOutBytes;
   constexpr uint32_t kEpiSmem = EpiCfg<TO>::kEpiSmem;
@@ -144,11 +145,13 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       uint32_t filled = 0;  // stages filled at least once
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      // stall_producer (failure-path test only): issue no loads, so the MMA
+      // warp's first wait on a full stage runs out after wait_ns.
+      for (int t = blockIdx.x; t < tiles && ok && !stall_producer; t += gridDim.x) {
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_SLOT)) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_SLOT, wait_ns)) {
             ok = false;
             break;
           }
@@ -196,14 +199,14 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       bool ok = true;
       bool issued = false;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_EPI)) {
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_EPI, wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&bars->full[stage], phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_TMA)) {
+          if (!mbar_wait(&bars->full[stage], phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_TMA, wait_ns)) {
             ok = false;
             break;
           }
@@ -268,7 +271,10 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
       ++tile_iter;
-      if (!mbar_wait(&bars->acc_full[acc], acc_phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_MMA)) break;
+      // (in the stall test the MMA warp's shorter wait gives up first)
+      if (!mbar_wait(&bars->acc_full[acc], acc_phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_MMA,
+                     stall_producer ? 4 * wait_ns : wait_ns))
+        break;
       tc_fence_after();
       const int row = mb * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
@@ -461,25 +467,20 @@ tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long 
   }
 }
 
-int g_sms = 0;
-
 template <typename TO, bool B_MN, bool TF32 = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
            const void* bias, int bias_dt, void* C,
            long long M, long long N, long long K, long long ldc, float alpha, int act,
-           uint32_t idesc, int vec_ok, cudaStream_t st) {
+           uint32_t idesc, int vec_ok, cudaStream_t st,
+           unsigned long long wait_ns = kWaitLimitNs, int stall_producer = 0) {
   auto kern = gemm_sm100_kernel<TO, B_MN, TF32>;
   const size_t smem = 1024 + EpiCfg<TO>::kRing * kStageBytes + EpiCfg<TO>::kEpiSmem + sizeof(GemmBarriers);
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  if (g_sms == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
-  }
+  const int sms = device_sm_count();
   const long long tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int grid = (int)(tiles < g_sms ? tiles : g_sms);
+  const int grid = (int)(tiles < sms ? tiles : sms);
   kern<<<grid, kThreads, smem, st>>>(ta, tb, tc, use_tma, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
-                                      alpha, act, idesc, vec_ok);
+                                      alpha, act, idesc, vec_ok, wait_ns, stall_producer);
   B2_CHECK_LAUNCH();
   return B2_OK;
 }
@@ -637,6 +638,34 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;
+}
+
+// Failure-path test: one fp16 tile GEMM (K-major A and B, fp16 C) whose TMA
+// producer is told to load nothing, with every wait bounded by wait_ns. The
+// MMA warp's wait for the first stage runs out, sets the CTA abort flag and
+// DEV_TIMEOUT_TMA in the status word; the epilogue leaves on the flag; TMEM is
+// freed and the kernel returns. Nothing is left in flight.
+int gemm_stall_test_launch(const void* A, const void* B, void* C, long long M, long long N,
+                           long long K, unsigned long long wait_ns, cudaStream_t st) {
+  CUtensorMap ta, tb, tc;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {kBK, kBM};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {kBK, kBN};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+  }
+  memset(&tc, 0, sizeof(tc));
+  const uint32_t idesc = idesc_f16(kBM, kBN, false, false, false);
+  return launch<__half, false>(ta, tb, tc, 0, nullptr, B2_F32, C, M, N, K, N, 1.f, B2_ACT_NONE, idesc,
+                               0, st, wait_ns, 1);
 }
 
 uint32_t gemm_read_status(bool clear) {

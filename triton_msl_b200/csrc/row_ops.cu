@@ -525,16 +525,7 @@ row_split_final_kernel(const Partial* __restrict__ ws, int splits, void* __restr
 }
 
 // -------------------------------------------------------------- dispatch
-int g_num_sms = 0;
-int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
+int num_sms() { return device_sm_count(); }
 
 template <typename T, int OP, int TPR, int VPT>
 int launch_reg(const void* x, const void* w, const void* b, void* out, long long rows, int cols,
@@ -701,12 +692,28 @@ namespace {
 constexpr long long kNoAllocMaxPartials = 16384;  // 16384 x 16 B = 256 KiB per device
 static __device__ __align__(256) Partial g_row_noalloc_scratch[kNoAllocMaxPartials];
 
-// Device address of the array, looked up once per device with that device
+// Device address of the array per device ordinal, looked up with that device
 // current (host code only sees a host-side stand-in under the array's name).
+// A successful lookup is cached; a failed one is not, so the next call tries
+// again. The mutex makes the first lookup safe from several host threads.
 constexpr int kNoAllocMaxDev = 64;
 Partial* g_noalloc_ptr[kNoAllocMaxDev];
-cudaError_t g_noalloc_err[kNoAllocMaxDev];
-std::once_flag g_noalloc_once[kNoAllocMaxDev];
+std::mutex g_noalloc_mu;
+
+cudaError_t noalloc_scratch(int dev, Partial** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_row_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *out = nullptr;
+      return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    }
+    g_noalloc_ptr[dev] = static_cast<Partial*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
 
 template <typename T, int OP>
 int noalloc_launch(const void* x, void* out, long long rows, long long cols, long long ldx,
@@ -773,20 +780,28 @@ int b2_row_reduce_noalloc(int op, const void* x, void* out, int64_t rows, int64_
     set_error("b2_row_reduce_noalloc: device ordinal %d out of range", dev);
     return B2_EINVAL;
   }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (st != nullptr) {
+    // The array's address is per device: the stream must belong to the
+    // current device, or the kernels would write another GPU's copy.
+    int sdev = dev;
+    if (cudaStreamGetDevice(st, &sdev) == cudaSuccess && sdev != dev) {
+      set_error("b2_row_reduce_noalloc: stream belongs to device %d but device %d is current", sdev, dev);
+      return B2_EINVAL;
+    }
+    cudaGetLastError();
+  }
   // First call on this device: resolve the array's device address (the
-  // current device is the one being set up).
-  std::call_once(g_noalloc_once[dev], [dev] {
-    void* p = nullptr;
-    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_row_noalloc_scratch);
-    g_noalloc_ptr[dev] = static_cast<Partial*>(p);
-  });
-  if (g_noalloc_err[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr) {
+  // current device is the one being set up). A failure is reported and
+  // retried on the next call.
+  Partial* scratch = nullptr;
+  const cudaError_t le = noalloc_scratch(dev, &scratch);
+  if (le != cudaSuccess) {
+    cudaGetLastError();
     set_error("b2_row_reduce_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-              cudaGetErrorString(g_noalloc_err[dev]));
+              cudaGetErrorString(le));
     return B2_ELAUNCH;
   }
-  Partial* scratch = g_noalloc_ptr[dev];
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case B2_F32: return noalloc_dispatch<float>(op, x, out, rows, cols, ld_x, scratch, splits, st);
     case B2_F16: return noalloc_dispatch<__half>(op, x, out, rows, cols, ld_x, scratch, splits, st);

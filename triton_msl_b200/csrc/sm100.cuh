@@ -69,10 +69,12 @@ __device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
 }
 
 // Bounded wait for phase `parity` of `bar` to complete. Gives up when the
-// CTA-wide abort flag is set by another waiter or after kWaitLimitNs, in which
-// case it sets the abort flag, ORs `why` into *status and returns false.
+// CTA-wide abort flag is set by another waiter or after limit_ns (default
+// kWaitLimitNs), in which case it sets the abort flag, ORs `why` into *status
+// and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t* status, uint32_t why) {
+                                          uint32_t* status, uint32_t why,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_addr(bar);
   if (mbar_test(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
@@ -80,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_test(a, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicOr(status, why);
         return false;

@@ -16,22 +16,28 @@ reference hands host buffers to its kernels the same way, driver.py:692+);
 from __future__ import annotations
 
 import math
+import threading
 from typing import Dict, Optional, Tuple
 
 import torch
 
 from . import ops
 
-_STREAMS: Dict[int, Tuple[torch.cuda.Stream, torch.cuda.Stream, torch.cuda.Stream]] = {}
+# Three side streams per (host thread, device): a thread's calls are ordered on
+# its own streams, and two threads never share (and so never interleave) them.
+_STREAMS: Dict[Tuple[int, int], Tuple[torch.cuda.Stream, torch.cuda.Stream, torch.cuda.Stream]] = {}
+_STREAMS_LOCK = threading.Lock()
 
 
 def _streams(dev: torch.device):
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    s = _STREAMS.get(idx)
-    if s is None:
-        with torch.cuda.device(idx):
-            s = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
-        _STREAMS[idx] = s
+    key = (threading.get_ident(), idx)
+    with _STREAMS_LOCK:
+        s = _STREAMS.get(key)
+        if s is None:
+            with torch.cuda.device(idx):
+                s = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
+            _STREAMS[key] = s
     return s
 
 
