@@ -3,15 +3,21 @@
 
 Headline: FlashAttention forward, fp16, causal,
 q/k/v [B=4, H=16, S=2048, D=128] ~ N(0,1)*0.5, TFLOP/s with causal FLOPs =
-2*B*H*S^2*D. The same run also measures the GEMM (8192^3 fp16 + bias + ReLU,
-TFLOP/s) and the row family (X[65536, 4096] fp32, GB/s), reported under
-"extra".
+2*B*H*S^2*D. The same run also measures, under "extra":
+  * the other BASELINE configs per rank (attention D=64/32, bf16, fp32;
+    GEMM 8192^3 fp16 + bias + ReLU and fp32 2048^3; the row family on
+    X[65536, 4096] fp32), each with its roofline and, at N=1, its CPU baseline;
+  * BASELINE config 5 as fixed total problems split across the ranks
+    ("scale_fa", "scale_gemm", "scale_rows_*": strong scaling, per-rank times,
+    efficiency against rank 0 timing the whole problem alone, and a sampled
+    oracle check per rank).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2|reference]
+  python bench.py --only fa_d64        # one configuration alone (ncu captures)
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same per-rank
-workload on its own shard of (batch, head) units ("weak" scaling, no data-path
-collective); value = all ranks' FLOPs / max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU): the headline runs the same per-rank
+workload on every rank ("weak" scaling, no data-path collective); value = all
+ranks' FLOPs / max-over-ranks device time.
 Timing: CUDA events around each launch on the launching stream; L2 (126 MB) is
 flushed by writing a 256 MB buffer between timed launches, outside the events.
 """
@@ -44,7 +50,8 @@ def load_peaks():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes from the committed ncu summary (kernel -> bytes)."""
+    """Per-launch DRAM bytes of each bench configuration (config name -> bytes), from
+    the committed ncu summaries (dram__bytes_read.sum + dram__bytes_write.sum)."""
     p = ROOT / "profiles" / "traffic.txt"
     out = {}
     if p.exists():
@@ -77,7 +84,7 @@ class ClockSampler:
         # launches).
         try:
             self._p = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",  # one index or "0,1,.."
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
@@ -124,9 +131,16 @@ class ClockSampler:
             for i, n in enumerate(names):
                 if len(s) > 5 + i and s[5 + i].lower().startswith("active"):
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(self.samples)}
+        per_gpu = {}
+        for s in self.samples:
+            if s[1].replace(".", "").isdigit():
+                per_gpu.setdefault(s[0], []).append(float(s[1]))
+        out = {"sm_mhz": statistics.median(mhz) if mhz else None,
+               "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+               "samples": len(self.samples)}
+        if len(per_gpu) > 1:
+            out["sm_mhz_per_gpu"] = {g: statistics.median(v) for g, v in sorted(per_gpu.items())}
+        return out
 
 
 def dist_setup(args):
@@ -188,24 +202,83 @@ def time_launches(fn, steps, warmup, flush_buf, world):
     return [a.elapsed_time(b) for a, b in evs]
 
 
-def cpu_sample_fa(cfg, seconds=8.0):
-    """Time the oracle (fp32 torch-CPU restatement of the reference's FA oracle)
-    on single (batch, head) slices of cfg; returns (TFLOP/s, threads, sample)."""
-    from oracle import oracle as O
-    from triton_msl_b200 import workloads as W
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    one = W.FAConfig("sample", 1, 1, cfg.S, cfg.D, cfg.causal, cfg.dtype, cfg.std)
-    q, k, v = W.fa_inputs(one, seed=1)
-    O.ref_attention(q, k, v, cfg.causal)  # warm-up
+# ------------------------------------------------------------------ CPU side
+def cpu_info(threads=None):
+    """(threads used, CPU model name) of this host."""
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return threads or os.cpu_count() or 1, model
+
+
+def cpu_rate(fn, units, seconds):
+    """Run fn (one warm-up, then repeatedly for >= `seconds`, at least twice);
+    returns (units per second, runs, elapsed s)."""
+    fn()
     n = 0
     t0 = time.perf_counter()
     while time.perf_counter() - t0 < seconds or n < 2:
-        O.ref_attention(q, k, v, cfg.causal)
+        fn()
         n += 1
     dt = time.perf_counter() - t0
-    tflops = one.flops() * n / dt / 1e12
-    return tflops, threads, f"{n} x one (b,h) head [1,1,{cfg.S},{cfg.D}] causal={cfg.causal} fp32 in {dt:.1f}s"
+    return units * n / dt, n, dt
+
+
+def cpu_baseline(value, unit, sample, threads, model, extrapolated=False):
+    d = {"value": value, "unit": unit, "cores": threads, "cpu_model": model, "kind": "port",
+         "sample": sample}
+    if extrapolated:
+        d["extrapolated"] = True
+    return d
+
+
+def cpu_fa(cfg, seconds, threads, model):
+    """Oracle attention on one (b, h) head of cfg (all of cfg when it is small)."""
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    heads = cfg.B * cfg.H if cfg.S * cfg.S * cfg.B * cfg.H <= (1 << 22) else 1
+    one = W.FAConfig("sample", 1, heads, cfg.S, cfg.D, cfg.causal, cfg.dtype, cfg.std)
+    q, k, v = W.fa_inputs(one, seed=1)
+    sm = 1.0 / 8 if cfg.dtype == torch.float32 else None
+    rate, n, dt = cpu_rate(lambda: O.ref_attention(q, k, v, cfg.causal, sm), one.flops(), seconds)
+    whole = heads == cfg.B * cfg.H
+    sample = (f"{n} x {'all' if whole else 'one (b,h) head of'} [{cfg.B},{cfg.H},{cfg.S},{cfg.D}] "
+              f"causal={cfg.causal}, fp32 torch-CPU oracle, {dt:.1f}s")
+    return cpu_baseline(round(rate / 1e12, 5), "TFLOP/s", sample, threads, model)
+
+
+def cpu_gemm(cfg, seconds, threads, model, rows=None):
+    """Oracle GEMM on the first `rows` rows of A (all when None), extrapolated per FLOP."""
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    import dataclasses
+    sub = cfg if rows is None or rows >= cfg.M else dataclasses.replace(cfg, M=rows)
+    a, bm, bias = W.gemm_inputs(sub, seed=1)
+    rate, n, dt = cpu_rate(lambda: O.ref_gemm(a, bm, bias, cfg.activation, cfg.out_dtype),
+                           sub.flops(), seconds)
+    sample = f"{n} x A[{sub.M},{sub.K}] @ B[{sub.K},{sub.N}] ({cfg.activation}), fp32 torch-CPU oracle, {dt:.1f}s"
+    return cpu_baseline(round(rate / 1e12, 5), "TFLOP/s", sample, threads, model,
+                        extrapolated=sub is not cfg)
+
+
+def cpu_rows(cfg, op, seconds, threads, model, rows=4096):
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    import dataclasses
+    sub = dataclasses.replace(cfg, rows=min(rows, cfg.rows))
+    x, w, b = W.row_inputs(sub, seed=1)
+    fn = {"softmax": lambda: O.ref_softmax(x), "layernorm": lambda: O.ref_layernorm(x, w, b, 1e-5),
+          "rmsnorm": lambda: O.ref_rmsnorm(x, w, 1e-6), "sum": lambda: O.ref_sum(x),
+          "max": lambda: O.ref_max(x), "argmax": lambda: O.ref_argmax(x)}[op]
+    rate, n, dt = cpu_rate(fn, sub.bytes(op), seconds)
+    sample = f"{n} x {op} over X[{sub.rows},{sub.cols}] fp32, torch-CPU oracle, {dt:.1f}s"
+    return cpu_baseline(round(rate / 1e9, 3), "GB/s", sample, threads, model,
+                        extrapolated=sub.rows != cfg.rows)
 
 
 def run_reference(args, world, rank):
@@ -216,7 +289,7 @@ def run_reference(args, world, rank):
     from triton_msl_b200 import workloads as W
     cfg = W.FA_F16_CAUSAL
     from oracle import oracle as O
-    threads = os.cpu_count() or 1
+    threads, model = cpu_info()
     torch.set_num_threads(threads)
     heads = 2
     samp = W.FAConfig("sample", 1, heads, cfg.S, cfg.D, cfg.causal, cfg.dtype, cfg.std)
@@ -239,16 +312,102 @@ def run_reference(args, world, rank):
         "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D,
                    "causal": True, "sample": sample},
         "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "cpu_model": model, "kind": "port", "sample": sample},
         "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def roofline(name, achieved, peak, unit, bound, traffic, per_launch_units, peak_kind):
-    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak,
+# ----------------------------------------------------------------- rooflines
+def fp32_ffma_peak_tflops(peaks):
+    """Nominal fp32 CUDA-core peak: 148 SMs x 128 FFMA lanes x 2 FLOP x max SM clock."""
+    return 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
+
+
+def mufu_ex2_peak(peaks):
+    """Nominal MUFU exponential rate: 16 ex2 / clk / SM x 148 SMs x max SM clock (per s)."""
+    return 16 * 148 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6
+
+
+def roofline(name, achieved, peak, unit, bound, traffic_bytes, peak_kind):
+    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 1),
             "unit": unit, "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-            "traffic": traffic.get(name) if traffic else None}
+            "traffic": traffic_bytes}
+
+
+def fa_roofline(kname, cfg, ms, peaks, peak_kind, traffic):
+    ach = cfg.flops() / (ms / 1e3) / 1e12
+    tb = traffic.get(cfg.name)
+    if kname == "fa_simt":
+        rl = roofline(kname, ach, fp32_ffma_peak_tflops(peaks), "TFLOP/s", "fp32-ffma", tb,
+                      "nominal fp32 FFMA (148 SM x 128 x 2 x sm_max_mhz)")
+    else:
+        rl = roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor", tb,
+                      peak_kind + " bf16 burst")
+        # second ceiling for the small head dims: one exponential per score
+        scores = cfg.B * cfg.H * (cfg.S * (cfg.S + 1) / 2 if cfg.causal else cfg.S * cfg.S)
+        rate = scores / (ms / 1e3)
+        rl["exp"] = {"scores_per_s": float(f"{rate:.4g}"), "mufu_ex2_per_s": float(f"{mufu_ex2_peak(peaks):.4g}"),
+                     "frac": round(rate / mufu_ex2_peak(peaks), 4),
+                     "note": "one exp per score; the kernel also computes part of them on the FMA pipe"}
+    return rl
+
+
+# ------------------------------------------------------------------- GPU arm
+def all_gather_floats(x: float, world: int):
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
+def time_one(fn, steps, warmup, flush, world):
+    """(max-over-ranks mean ms, per-rank mean ms)."""
+    ms = statistics.mean(time_launches(fn, steps, warmup, flush, world))
+    per = all_gather_floats(ms, world)
+    return max(per), per
+
+
+def measure_link(h2d_bytes, d2h_bytes, dev, world, steps=5):
+    """Plain pinned host<->device copies of one e2e step's byte counts: alone and
+    both directions at once on two streams (what the e2e pipeline overlaps),
+    timed on the device, max over ranks (all ranks copy at the same time)."""
+    hin = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    hout = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    din = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    dout = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def run(mode):
+        torch.cuda.synchronize()
+        barrier(world)
+        cur = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        s1.wait_stream(cur)
+        s2.wait_stream(cur)
+        for _ in range(steps):
+            if mode in ("h2d", "both"):
+                with torch.cuda.stream(s1):
+                    din.copy_(hin, non_blocking=True)
+            if mode in ("d2h", "both"):
+                with torch.cuda.stream(s2):
+                    hout.copy_(dout, non_blocking=True)
+        cur.wait_stream(s1)
+        cur.wait_stream(s2)
+        b.record(cur)
+        torch.cuda.synchronize()
+        return max(all_gather_floats(a.elapsed_time(b) / steps, world))
+
+    run("both")  # warm-up
+    h2d_ms, d2h_ms, both_ms = run("h2d"), run("d2h"), run("both")
+    del hin, hout, din, dout
+    return {"h2d_gbs_per_gpu": round(h2d_bytes / (h2d_ms / 1e3) / 1e9, 1),
+            "d2h_gbs_per_gpu": round(d2h_bytes / (d2h_ms / 1e3) / 1e9, 1),
+            "both_ms": round(both_ms, 4)}
 
 
 def run_b2(args, world, rank, local):
@@ -258,6 +417,9 @@ def run_b2(args, world, rank, local):
     peaks, peak_kind = load_peaks()
     traffic = load_traffic()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    threads, model = cpu_info()
+    do_cpu = rank == 0 and world == 1 and not args.no_cpu
+    torch.set_num_threads(max(1, threads // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", world)))))
 
     # ---------------- headline: FA fp16 causal D=128 ----------------
     cfg = W.FA_F16_CAUSAL
@@ -267,63 +429,76 @@ def run_b2(args, world, rank, local):
     kern = b2.last_kernel()
     if kern != "fa_sm100":
         raise RuntimeError(f"headline FA ran on {kern}, not the tensor-core kernel")
-    # Clock sampling starts first and the sampler's start-up is over (first sample
-    # in, at most 5 s) before anything is timed. No extended pre-warm: on these
-    # parts the idle SM clock is already the maximum, and a sub-second loop of
-    # back-to-back launches before the timed steps tripped the power cap
-    # (clocks down to ~1590 MHz for the timed steps that followed).
-    sampler = ClockSampler(local) if rank == 0 else None
+    # Rank 0 samples the clocks of every GPU of the job from before the first
+    # timed step to the end of the GPU work (the headline's own timed region is
+    # a few milliseconds, shorter than one 200 ms sample). No extended pre-warm:
+    # the idle SM clock is already the maximum, and a sub-second loop of
+    # back-to-back launches before the timed steps tripped the power cap.
+    sampler = ClockSampler(",".join(str(i) for i in range(world)) if world > 1 else local) \
+        if rank == 0 else None
     if sampler:
         sampler.__enter__()
         sampler.wait_first(5.0)
     try:
         times = time_launches(fa, args.steps, args.warmup, flush, world)
+        ms_rank = statistics.mean(times)
+        per_rank = all_gather_floats(ms_rank, world)
+        ms = max(per_rank)
+        flops = cfg.flops()
+        value = world * flops / (ms / 1e3) / 1e12
+        rl = fa_roofline("fa_sm100", cfg, ms, peaks, peak_kind, traffic)
+
+        # e2e through the public host-tensor entry point: every step copies q, k, v
+        # from pinned host memory, runs the kernel and reads o back, chunk-pipelined
+        # over (batch, head) on three streams (copies both ways overlap the kernel)
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        ho = torch.empty_like(hq).pin_memory()
+
+        def e2e_step():
+            b2.flash_attn_fwd_host(hq, hk, hv, causal=True, out=ho)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        st = torch.cuda.current_stream()
+        a = torch.cuda.Event(enable_timing=True)
+        bev = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(args.steps):
+            e2e_step()
+        bev.record(st)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_per_rank = all_gather_floats(a.elapsed_time(bev) / args.steps, world)
+        e2e_ms = max(e2e_per_rank)
+        e2e_val = world * flops / (e2e_ms / 1e3) / 1e12
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+        d2h = ho.numel() * ho.element_size()
+        del hq, hk, hv, ho, q, k, v
+        link = measure_link(h2d, d2h, dev, world)
+        link["e2e_ms"] = round(e2e_ms, 4)
+        link["e2e_frac_of_link"] = round(link["both_ms"] / e2e_ms, 4)
+        link["note"] = ("e2e is bounded by the host link: both_ms = the step's host->device and "
+                        "device->host bytes as plain pinned copies, both directions at once, "
+                        "all ranks at once")
+
+        extra = {}
+        if not args.headline_only:
+            extra = run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
+                               threads, model)
+            extra.update(run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
+                                   threads, model))
     finally:
         if sampler:
             sampler.__exit__()
-    ms_rank = statistics.mean(times)
-    ms = max_over_ranks(ms_rank, world)
-    flops = cfg.flops()
-    value = world * flops / (ms / 1e3) / 1e12
-    peak_tc = float(peaks["bf16_tflops"])
-    rl = roofline("fa_sm100", flops / (ms / 1e3) / 1e12, peak_tc, "TFLOP/s", "tensor", traffic,
-                  1, peak_kind)
-
-    # e2e through the public host-tensor entry point: every step copies q, k, v from
-    # pinned host memory, runs the kernel and reads o back, chunk-pipelined over
-    # (batch, head) on three streams (copies in both directions overlap the kernel)
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    ho = torch.empty_like(hq).pin_memory()
-    def e2e_step():
-        b2.flash_attn_fwd_host(hq, hk, hv, causal=True, out=ho)
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    st = torch.cuda.current_stream()
-    a = torch.cuda.Event(enable_timing=True)
-    bev = torch.cuda.Event(enable_timing=True)
-    a.record(st)
-    for _ in range(args.steps):
-        e2e_step()
-    bev.record(st)
-    torch.cuda.synchronize()
-    barrier(world)
-    e2e_ms = max_over_ranks(a.elapsed_time(bev) / args.steps, world)
-    e2e_val = world * flops / (e2e_ms / 1e3) / 1e12
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
-    d2h = ho.numel() * ho.element_size()
-    del hq, hk, hv, ho
-
-    extra = {}
-    launches = args.steps  # headline timed region: one fa_sm100 launch per step
-    if not args.headline_only:
-        extra = run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic)
 
     if rank != 0:
         return
     clocks = sampler.summary() if sampler else None
-    cpu_val, cores, sample = cpu_sample_fa(cfg, seconds=args.cpu_seconds)
+    threads_all, _ = cpu_info()
+    torch.set_num_threads(threads_all)
+    cb = cpu_fa(cfg, args.cpu_seconds if world == 1 else 3.0, threads_all, model)
     line = {
         "metric": "fa_fwd_fp16_causal_d128_tflops", "value": round(value, 2), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -333,70 +508,83 @@ def run_b2(args, world, rank, local):
                    "causal": True, "flops_per_step_per_gpu": flops,
                    "l2": "flushed between timed launches (256 MB write)",
                    "parallelism": f"(batch,head) shards x{world}, no collective"},
+        "per_rank_ms": [round(x, 4) for x in per_rank],
         "roofline": rl,
-        "cpu_baseline": {"value": round(cpu_val, 5), "unit": "TFLOP/s", "cores": cores,
-                         "kind": "port", "sample": sample},
+        "cpu_baseline": cb,
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches,
+                "d2h_bytes_per_step": d2h, "per_rank_ms": [round(x, 4) for x in e2e_per_rank],
+                "link": link},
+        "gpu_launches": args.steps,  # headline timed region: one fa_sm100 launch per step
         "clocks": clocks,
         "extra": extra,
     }
     print(json.dumps(line), flush=True)
 
 
-def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic):
-    """GEMM 8192^3 + bias + ReLU and the row family at 65536x4096, same timing rules."""
+def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, threads, model):
+    """The other BASELINE configs (attention D=64/32, bf16, fp32; GEMM 8192^3 +
+    bias + ReLU and fp32 2048^3; the row family at 65536x4096), per-rank
+    weak-scaling copies, same timing rules, each with its roofline, its own
+    ncu traffic and (N=1, rank 0) its CPU baseline."""
     import triton_msl_b200 as b2
     from triton_msl_b200 import workloads as W
     out = {}
     steps = max(3, min(args.steps, 10))
-    # the other attention configs of BASELINE (head dims 64 / 32, bf16, fp32)
-    for cfg, kw in ((W.FA_F16_CAUSAL_D64, {}), (W.FA_F16_CAUSAL_D32, {}),
-                    (W.FAConfig("fa_bf16_causal_B4_H16_S2048_D128", 4, 16, 2048, 128, True,
-                                torch.bfloat16, 0.5), {}),
-                    (W.FA_F32, {"sm_scale": 1 / 8})):
+    cs = args.cpu_seconds_extra
+    fa_cfgs = ((W.FA_F16_CAUSAL_D64, {}), (W.FA_F16_CAUSAL_D32, {}), (W.FA_BF16_CAUSAL, {}),
+               (W.FA_F32, {"sm_scale": 1 / 8}))
+    for cfg, kw in fa_cfgs:
         q, k, v = W.fa_inputs(cfg, device=dev, seed=rank)
         fn = lambda: b2.flash_attn_fwd(q, k, v, causal=cfg.causal, **kw)
         fn()
         kname = b2.last_kernel()
-        ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+        ms, per = time_one(fn, steps, 3, flush, world)
         ach = cfg.flops() / (ms / 1e3) / 1e12
-        out[cfg.name] = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
-                         "kernel": kname,
-                         "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s",
-                                              "tensor", traffic, 1, peak_kind)}
+        e = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+             "per_rank_ms": [round(x, 4) for x in per], "kernel": kname,
+             "roofline": fa_roofline(kname, cfg, ms, peaks, peak_kind, traffic)}
+        if do_cpu:
+            e["cpu_baseline"] = cpu_fa(cfg, cs, threads, model)
+        out[cfg.name] = e
         del q, k, v
     g32 = W.GEMM_F32
     a32, b32, _ = W.gemm_inputs(g32, device=dev, seed=rank)
     fn = lambda: b2.gemm(a32, b32)
     fn()
     kname = b2.last_kernel()
-    ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+    ms, per = time_one(fn, steps, 3, flush, world)
     ach32 = g32.flops() / (ms / 1e3) / 1e12
-    out[g32.name] = {"value": round(world * ach32, 2), "unit": "TFLOP/s",
-                     "ms": round(ms, 4), "kernel": kname}
+    e = {"value": round(world * ach32, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+         "per_rank_ms": [round(x, 4) for x in per], "kernel": kname}
     if kname == "gemm_sm100_tf32x3":
         # fp32 product as 3xTF32 (split pass + one tensor-core GEMM over 3K): the
         # tensor pipe does 3x the listed FLOPs at the tf32 rate, taken as half the
         # measured bf16 rate (the nominal dense ratio, 1.1 vs 2.25 PFLOP/s)
-        out[g32.name]["roofline"] = roofline(kname, 3 * ach32, float(peaks["bf16_tflops"]) / 2,
-                                             "TFLOP/s", "tensor", traffic, 1, peak_kind)
-        out[g32.name]["note"] = ("3xTF32 on tensor cores (max-abs 1e-4 met); roofline counts the "
-                                 "3 tf32 products against tf32 peak = measured bf16 / 2")
+        e["roofline"] = roofline(kname, 3 * ach32, float(peaks["bf16_tflops"]) / 2, "TFLOP/s",
+                                 "tensor", traffic.get(g32.name), peak_kind + " bf16 burst / 2")
+        e["note"] = ("3xTF32 on tensor cores (max-abs 1e-4 met); achieved counts the 3 tf32 "
+                     "products, against tf32 peak = measured bf16 / 2; split launches included")
     else:
-        out[g32.name]["note"] = "fp32 FFMA path (1e-4 bound); B200 dense fp32 is ~80 TFLOP/s nominal"
+        e["roofline"] = roofline(kname, ach32, fp32_ffma_peak_tflops(peaks), "TFLOP/s", "fp32-ffma",
+                                 traffic.get(g32.name), "nominal fp32 FFMA")
+    if do_cpu:
+        e["cpu_baseline"] = cpu_gemm(g32, cs, threads, model)
+    out[g32.name] = e
     del a32, b32
     g = W.GEMM_F16
     a, bm, bias = W.gemm_inputs(g, device=dev, seed=rank)
     fn = lambda: b2.gemm(a, bm, bias, "relu", torch.float16)
     fn()
     kname = b2.last_kernel()
-    ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+    ms, per = time_one(fn, steps, 3, flush, world)
     ach = g.flops() / (ms / 1e3) / 1e12
-    out[g.name] = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
-                   "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s",
-                                        "tensor", traffic, 1, peak_kind)}
+    e = {"value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+         "per_rank_ms": [round(x, 4) for x in per], "kernel": kname,
+         "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor",
+                              traffic.get(g.name), peak_kind + " bf16 burst")}
+    if do_cpu:
+        e["cpu_baseline"] = cpu_gemm(g, cs, threads, model, rows=256)
+    out[g.name] = e
     del a, bm, bias
     r = W.ROWS_F32
     x, w, bb = W.row_inputs(r, device=dev, seed=rank)
@@ -408,69 +596,211 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic):
     for op, fn in ops.items():
         fn()
         kname = b2.last_kernel()
-        ms = max_over_ranks(statistics.mean(time_launches(fn, steps, 3, flush, world)), world)
+        ms, per = time_one(fn, steps, 3, flush, world)
         gbs = r.bytes(op) / (ms / 1e3) / 1e9
-        out[f"{r.name}_{op}"] = {"value": round(world * gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
-                                 "roofline": roofline(f"{kname}_{op}", gbs, float(peaks["hbm_gbs"]),
-                                                      "GB/s", "hbm", traffic, 1, peak_kind)}
+        e = {"value": round(world * gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
+             "per_rank_ms": [round(x_, 4) for x_ in per], "kernel": kname,
+             "roofline": roofline(f"{kname}_{op}", gbs, float(peaks["hbm_gbs"]), "GB/s", "hbm",
+                                  traffic.get(f"{r.name}_{op}"), peak_kind + " copy")}
+        if do_cpu:
+            e["cpu_baseline"] = cpu_rows(r, op, cs, threads, model)
+        out[f"{r.name}_{op}"] = e
+    del x, w, bb
     return out
 
 
-def run_scale(args, world, rank, local):
-    """a fixed total problem split across the ranks with no
-    collective (strong scaling). scale-fa: FA bf16 causal [64,32,8192,128] by
-    (batch, head); scale-gemm: GEMM bf16 65536x16384x16384 by 128-row M-tiles
-    (B replicated). Each rank builds only its own shard, on its own GPU."""
+def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, threads, model):
+    """BASELINE config 5 and the row family as fixed total problems split across
+    the ranks with no collective (strong scaling): FA bf16 causal [64,32,8192,128]
+    by (batch, head), GEMM bf16 65536x16384x16384 by 128-row M-tiles (B built on
+    every rank from one seed: a replicated local copy), rows 65536x4096 fp32
+    (softmax, argmax) by rows. Each rank builds only its own shard, on its own
+    GPU. value = total work / max-over-ranks time; efficiency = T(1) / (N T(N)),
+    T(1) timed by rank 0 alone on the whole problem in the same run (at N=1 the
+    shard is the whole problem). A sampled (b,h) head, row block of C and row
+    block of X per rank is checked against the CPU oracle."""
     import math
     import triton_msl_b200 as b2
+    from oracle import oracle as O
     from triton_msl_b200 import shard, workloads as W
-    dev = torch.device("cuda", torch.cuda.current_device())
-    peaks, peak_kind = load_peaks()
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    if args.config == "scale-fa":
-        cfg = W.FA_BF16_SCALE
-        lo, hi = shard.unit_range(cfg.B * cfg.H, world, rank)
-        n = hi - lo
-        q, k, v = ((torch.randn((1, n, cfg.S, cfg.D), generator=g, device=dev) * cfg.std)
-                   .to(cfg.dtype) for _ in range(3))
-        fn = lambda: b2.flash_attn_fwd(q, k, v, causal=True)
-        flops_local = cfg.flops() * n / (cfg.B * cfg.H)
-        total = cfg.flops()
-        metric, workload = "fa_fwd_bf16_causal_d128_tflops", cfg.name
-        conf = {"B": cfg.B, "H": cfg.H, "S": cfg.S, "D": cfg.D, "causal": True,
-                "units_this_rank": n}
-    else:
-        cfg = W.GEMM_BF16_SCALE
-        lo, hi = shard.unit_range(cfg.M, world, rank, align=128)
-        s_ = 1.0 / math.sqrt(cfg.K)
-        a = (torch.randn((hi - lo, cfg.K), generator=g, device=dev) * s_).to(cfg.dtype)
-        bm = (torch.randn((cfg.K, cfg.N), generator=g, device=dev) * s_).to(cfg.dtype)
-        fn = lambda: b2.gemm(a, bm)
-        flops_local = 2.0 * (hi - lo) * cfg.N * cfg.K
-        total = cfg.flops()
-        metric, workload = "gemm_bf16_tflops", cfg.name
-        conf = {"M": cfg.M, "N": cfg.N, "K": cfg.K, "rows_this_rank": hi - lo}
+    out = {}
+    sus = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    steps = max(3, min(args.steps, 10))
+
+    def finish(name, metric_unit, total, shard_work, ms, per, full_ms, kname, err, tol, extra):
+        eff = full_ms / (world * ms) if full_ms else None
+        if metric_unit == "TFLOP/s":
+            per_gpu = shard_work / (ms / 1e3) / 1e12
+            rl = roofline(kname, per_gpu, sus, "TFLOP/s", "tensor", traffic.get(name),
+                          peak_kind + " bf16 sustained (a step of tens of ms runs under the power cap)")
+            val = total / (ms / 1e3) / 1e12
+        else:
+            per_gpu = shard_work / (ms / 1e3) / 1e9
+            rl = roofline(kname, per_gpu, float(peaks["hbm_gbs"]), "GB/s", "hbm", traffic.get(name),
+                          peak_kind + " copy")
+            val = total / (ms / 1e3) / 1e9
+        e = {"value": round(val, 2), "unit": metric_unit, "n_gpus": world, "scaling": "strong",
+             "ms": round(ms, 4), "per_rank_ms": [round(x, 4) for x in per],
+             "full_problem_ms_1gpu": round(full_ms, 4) if full_ms else None,
+             "efficiency": round(eff, 4) if eff else None, "kernel": kname,
+             "roofline_per_gpu": rl,
+             "oracle_check": {"max_err_over_ranks": float(f"{err:.3e}"), "tol": tol, "ok": err <= tol},
+             "parallelism": f"shards x{world}, no collective"}
+        e.update(extra)
+        return e
+
+    def full_time(build, fn_of):
+        """Rank 0 alone times the whole problem (others wait at the barrier)."""
+        if world == 1:
+            return None
+        res = None
+        if rank == 0:
+            objs = build()
+            fn = fn_of(objs)
+            fn()
+            res = statistics.mean(time_launches(fn, steps, 3, flush, 1))
+            del objs, fn
+            torch.cuda.empty_cache()
+        barrier(world)
+        return max(all_gather_floats(res or 0.0, world))
+
+    # ---------------------------------------------------------------- FA
+    cfg = W.FA_BF16_SCALE
+    lo, hi = shard.unit_range(cfg.B * cfg.H, world, rank)
+    n = hi - lo
+
+    def fa_build(units, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        return [(torch.randn((1, units, cfg.S, cfg.D), generator=g, device=dev) * cfg.std).to(cfg.dtype)
+                for _ in range(3)]
+
+    q, k, v = fa_build(n, 1000 + rank)
+    fn = lambda: b2.flash_attn_fwd(q, k, v, causal=True)
     fn()
     kname = b2.last_kernel()
-    times = time_launches(fn, args.steps, args.warmup, flush, world)
-    ms = max_over_ranks(statistics.mean(times), world)
-    if rank != 0:
-        return
-    print(json.dumps({
-        "metric": metric, "value": round(total / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": workload, **conf, "parallelism": f"shards x{world}, no collective",
-                   "l2": "flushed between timed launches (256 MB write)"},
-        # a step of this size runs tens of milliseconds under the power cap: the
-        # sustained GEMM figure is the denominator, not the burst one
-        "roofline": roofline(kname, flops_local / (ms / 1e3) / 1e12,
-                             float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])),
-                             "TFLOP/s", "tensor", {}, 1, peak_kind + " (sustained)"),
-        "gpu_launches": args.steps,
-    }), flush=True)
+    ms, per = time_one(fn, steps, args.warmup, flush, world)
+    o = fn()
+    i = n // 2
+    ref = O.ref_attention(q[:, i:i + 1].cpu(), k[:, i:i + 1].cpu(), v[:, i:i + 1].cpu(), True)
+    err = max(all_gather_floats(O.normwise_err(o[:, i:i + 1], ref), world))
+    del q, k, v, o
+    full = full_time(lambda: fa_build(cfg.B * cfg.H, 999),
+                     lambda t: (lambda: b2.flash_attn_fwd(t[0], t[1], t[2], causal=True)))
+    e = finish(cfg.name, "TFLOP/s", cfg.flops(), cfg.flops() * n / (cfg.B * cfg.H), ms, per, full,
+               kname, err, O.TOL_LOWP_REL + 2.0 ** -8, {"units_rank0": n})
+    if do_cpu:
+        e["cpu_baseline"] = cpu_fa(cfg, args.cpu_seconds_extra, threads, model)
+    out["scale_fa"] = e
+
+    # -------------------------------------------------------------- GEMM
+    gc = W.GEMM_BF16_SCALE
+    lo, hi = shard.unit_range(gc.M, world, rank, align=128)
+    s_ = 1.0 / math.sqrt(gc.K)
+
+    def gemm_build(rows, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        a = (torch.randn((rows, gc.K), generator=g, device=dev) * s_).to(gc.dtype)
+        g2 = torch.Generator(device=dev).manual_seed(4242)   # B: the same on every rank
+        bm = (torch.randn((gc.K, gc.N), generator=g2, device=dev) * s_).to(gc.dtype)
+        return a, bm
+
+    a, bm = gemm_build(hi - lo, 2000 + rank)
+    fn = lambda: b2.gemm(a, bm)
+    fn()
+    kname = b2.last_kernel()
+    ms, per = time_one(fn, steps, args.warmup, flush, world)
+    c = fn()
+    r0 = (hi - lo) // 2
+    ref = O.ref_gemm(a[r0:r0 + 32].cpu(), bm.cpu(), None, "none", torch.bfloat16)
+    err = max(all_gather_floats(O.normwise_err(c[r0:r0 + 32], ref), world))
+    del a, bm, c
+    torch.cuda.empty_cache()
+    full = full_time(lambda: gemm_build(gc.M, 1999), lambda t: (lambda: b2.gemm(t[0], t[1])))
+    e = finish(gc.name, "TFLOP/s", gc.flops(), 2.0 * (hi - lo) * gc.N * gc.K, ms, per, full, kname,
+               err, O.TOL_LOWP_REL + 2.0 ** -8, {"rows_rank0": hi - lo})
+    if do_cpu:
+        e["cpu_baseline"] = cpu_gemm(gc, args.cpu_seconds_extra, threads, model, rows=64)
+    out["scale_gemm"] = e
+
+    # -------------------------------------------------------------- rows
+    rc = W.ROWS_F32
+    lo, hi = shard.unit_range(rc.rows, world, rank)
+    import dataclasses
+    for op in ("softmax", "argmax"):
+        def rows_build(nrows, seed):
+            return (torch.randn((nrows, rc.cols), generator=torch.Generator(device=dev).manual_seed(seed),
+                                device=dev),)
+        (x,) = rows_build(hi - lo, 3000 + rank)
+        f = b2.row_softmax if op == "softmax" else b2.row_argmax
+        fn = lambda: f(x)
+        fn()
+        kname = b2.last_kernel()
+        ms, per = time_one(fn, steps, args.warmup, flush, world)
+        y = fn()
+        xs = x[:256].cpu()
+        if op == "softmax":
+            err = O.max_abs_err(y[:256], O.ref_softmax(xs))
+            tol = O.TOL_F32_ABS
+        else:
+            err = 0.0 if torch.equal(y[:256].cpu(), O.ref_argmax(xs)) else 1.0
+            tol = 0.0
+        err = max(all_gather_floats(err, world))
+        del x, y
+        full = full_time(lambda: rows_build(rc.rows, 2999), lambda t: (lambda: f(t[0])))
+        sub = dataclasses.replace(rc, rows=hi - lo)
+        e = finish(f"{rc.name}_{op}", "GB/s", rc.bytes(op), sub.bytes(op), ms, per, full, kname,
+                   err, tol, {"rows_rank0": hi - lo})
+        if do_cpu:
+            e["cpu_baseline"] = cpu_rows(rc, op, args.cpu_seconds_extra, threads, model)
+        out[f"scale_rows_{op}"] = e
+    return out
+
+
+ONLY = ("headline", "fa_d64", "fa_d32", "fa_bf16", "fa_f32", "gemm_f16", "gemm_f32",
+        "rows_softmax", "rows_layernorm", "rows_rmsnorm", "rows_sum", "rows_max", "rows_argmax",
+        "gemm_bf16_scale_shard")
+
+
+def run_only(args):
+    """One configuration in a process that allocates only its inputs (for ncu
+    captures: one kernel family, a few launches, a few GB on the device)."""
+    import triton_msl_b200 as b2
+    from triton_msl_b200 import workloads as W
+    dev = torch.device("cuda", 0)
+    name = args.only
+    if name.startswith("fa_") or name == "headline":
+        cfg = {"headline": W.FA_F16_CAUSAL, "fa_d64": W.FA_F16_CAUSAL_D64, "fa_d32": W.FA_F16_CAUSAL_D32,
+               "fa_bf16": W.FA_BF16_CAUSAL, "fa_f32": W.FA_F32}[name]
+        q, k, v = W.fa_inputs(cfg, device=dev)
+        kw = {"sm_scale": 1 / 8} if cfg.dtype == torch.float32 else {}
+        fn = lambda: b2.flash_attn_fwd(q, k, v, causal=cfg.causal, **kw)
+        work, unit = cfg.flops(), "TFLOP/s"
+    elif name in ("gemm_f16", "gemm_f32"):
+        cfg = W.GEMM_F16 if name == "gemm_f16" else W.GEMM_F32
+        a, bm, bias = W.gemm_inputs(cfg, device=dev)
+        fn = (lambda: b2.gemm(a, bm, bias, "relu", torch.float16)) if name == "gemm_f16" \
+            else (lambda: b2.gemm(a, bm))
+        work, unit = cfg.flops(), "TFLOP/s"
+    elif name == "gemm_bf16_scale_shard":
+        cfg = W.GEMM_BF16_SCALE
+        a = torch.randn(8192, cfg.K, device=dev).to(cfg.dtype)
+        bm = torch.randn(cfg.K, cfg.N, device=dev).to(cfg.dtype)
+        fn = lambda: b2.gemm(a, bm)
+        work, unit = 2.0 * 8192 * cfg.N * cfg.K, "TFLOP/s"
+    else:
+        op = name.split("_", 1)[1]
+        r = W.ROWS_F32
+        x, w, bb = W.row_inputs(r, device=dev)
+        fn = {"softmax": lambda: b2.row_softmax(x), "layernorm": lambda: b2.row_layernorm(x, w, bb, 1e-5),
+              "rmsnorm": lambda: b2.row_rmsnorm(x, w, 1e-6), "sum": lambda: b2.row_sum(x),
+              "max": lambda: b2.row_max(x), "argmax": lambda: b2.row_argmax(x)}[op]
+        work, unit = r.bytes(op), "GB/s"
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    fn()
+    ms = statistics.median(time_launches(fn, args.steps, args.warmup, flush, 1))
+    rate = work / (ms / 1e3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"only": name, "kernel": b2.last_kernel(), "ms_median": round(ms, 4),
+                      "value": round(rate, 2), "unit": unit, "steps": args.steps}), flush=True)
 
 
 def main():
@@ -480,18 +810,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--headline-only", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--config", default="headline", choices=["headline", "scale-fa", "scale-gemm"],
-                    help="headline: BASELINE configs[1] (+ extras); scale-*: BASELINE config 5")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines of the extras")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline sample length of the headline")
+    ap.add_argument("--cpu-seconds-extra", type=float, default=1.5,
+                    help="CPU-baseline sample length of each extra configuration")
+    ap.add_argument("--only", choices=ONLY, default=None,
+                    help="time one configuration alone (1 GPU; small process for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.only:
+        run_only(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
-        elif args.config != "headline":
-            run_scale(args, world, rank, local)
         else:
             run_b2(args, world, rank, local)
     finally:

@@ -72,8 +72,9 @@ const char* b2_version(void);
 const char* b2_last_error(void);
 
 /* Kernel family the calling thread's last successful call launched
- * ("fa_sm100", "fa_simt", "gemm_sm100", "gemm_simt", "row_reduce", "row_split",
- * "row_memset"). Introspection for tests and benchmarks; the reference's
+ * ("fa_sm100", "fa_simt", "gemm_sm100" (128x256 tiles), "gemm_sm100_n128"
+ * (128x128 tiles), "gemm_sm100_splitk", "gemm_sm100_tf32x3", "gemm_simt",
+ * "row_reduce", "row_split", "row_memset"). Introspection for tests and benchmarks; the reference's
  * equivalent is its TRITON_MSL_PATH_LOG lowering-path log
  * (triton_msl/codegen/msl_emitter.py:523-538). */
 const char* b2_last_kernel(void);
@@ -111,6 +112,12 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o,
  * (x = hi + lo, A.B = hi.hi + hi.lo + lo.hi; no input rounding to TF32
  * alone; the tensor core's fp32 accumulation adds an error that grows with K,
  * measured 2.5e-5 * max|C| at K=2048); with no workspace, fp32 FMA.
+ * fp16/bf16 inputs: the tile width (128x256 or 128x128) follows the SM count
+ * (the narrower tile when the last wave of wide tiles would leave more SMs
+ * idle); when even narrow tiles would fill at most half the SMs and K >= 512,
+ * the K loop is split across CTAs (split-K) given the workspace
+ * b2_query_workspace reports, with fp32 partial sums reduced in a fixed order
+ * before the epilogue (without the workspace the unsplit kernel runs).
  * workspace/ws_bytes: scratch as reported by b2_query_workspace (may be NULL/0
  * when that reports 0, or to force the FMA path for fp32).
  */

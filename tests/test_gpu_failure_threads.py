@@ -53,7 +53,7 @@ def test_bounded_wait_expires_and_reports(shape):
     # the context is still usable and a normal call matches the oracle
     ref = O.ref_gemm(a.cpu(), bt.cpu().t(), None, "none", torch.float16)
     got = b2.gemm(a, bt.t(), None, "none", torch.float16)
-    assert b2.last_kernel() == "gemm_sm100"
+    assert b2.last_kernel().startswith("gemm_sm100")
     assert O.normwise_err(got, ref) <= O.TOL_LOWP_REL
     assert _lib.device_status(dev, clear=True) == 0
 

@@ -21,7 +21,9 @@ int gemm_simt_launch(const void*, const void*, const void*, void*, long long, lo
 bool gemm_sm100_eligible(const void*, const void*, long long, long long, long long,
                          const int64_t*, int);
 int gemm_sm100_launch(const void*, const void*, const void*, void*, long long, long long,
-                      long long, const int64_t*, float, int, int, int, int, cudaStream_t);
+                      long long, const int64_t*, float, int, int, int, int, void*, size_t, cudaStream_t,
+                      int*);
+size_t gemm_f16_workspace(long long, long long, long long, int);
 size_t gemm_tf32x3_workspace(long long, long long, long long);
 int gemm_tf32x3_launch(const float*, const float*, const void*, void*, long long, long long,
                        long long, const int64_t*, float, int, int, int, void*, cudaStream_t);
@@ -195,9 +197,11 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
                             bias, C, M, N, K, strides, alpha, act, bias_dtype, out_dtype, workspace, st);
     if (rc == B2_OK) t_kernel = "gemm_sm100_tf32x3";
   } else if (tc) {
+    int variant = 0;
     rc = gemm_sm100_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
-                           out_dtype, st);
-    if (rc == B2_OK) t_kernel = "gemm_sm100";
+                           out_dtype, workspace, ws_bytes, st, &variant);
+    if (rc == B2_OK)
+      t_kernel = variant == 2 ? "gemm_sm100_splitk" : variant == 1 ? "gemm_sm100_n128" : "gemm_sm100";
   } else {
     rc = gemm_simt_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
                           out_dtype, st);
@@ -257,7 +261,10 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out, in
 size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3) {
   (void)a3;
   switch (kind) {
-    case 0: return (a3 == B2_F32 && device_is_sm100()) ? gemm_tf32x3_workspace(a0, a1, a2) : 0;
+    case 0:
+      if (!device_is_sm100()) return 0;
+      if (a3 == B2_F32) return gemm_tf32x3_workspace(a0, a1, a2);
+      return gemm_f16_workspace(a0, a1, a2, B2_ACT_NONE);
     case 1: return row_op_workspace((int)a0, a1, a2);
     case 2: return 0;
     default: return 0;

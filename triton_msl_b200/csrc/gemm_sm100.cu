@@ -32,26 +32,32 @@ using namespace sm100;
 
 __device__ uint32_t g_gemm_status;
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kBM = 128, kBK = 64, kMaxStages = 6;
 constexpr int kThreads = 192;
 constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr int kGroupM = 16;                    // raster: 16 M-tiles per group
-constexpr uint32_t kTmemCols = 512;
+#ifndef B2_GEMM_GROUP_M
+#define B2_GEMM_GROUP_M 16
+#endif
+constexpr int kGroupM = B2_GEMM_GROUP_M;      // raster: M-tiles per group
+// Per tile width BN (256, or 128 when that fills the SMs better): B stage
+// bytes, and two BN-column fp32 accumulators in TMEM.
 // Epilogue staging: per epilogue warp two 32x32 output blocks, written
 // swizzled and sent to global memory with TMA tensor stores, plus two bias
-// tiles. With fp32 output the blocks are twice as large, so that variant uses
-// a 3-stage operand ring to stay inside 227 KB of shared memory.
-template <typename TO> struct EpiCfg {
-  static constexpr int kRing = sizeof(TO) == 4 ? 3 : 4;
+// tiles. The operand ring takes what is left of 227 KB of shared memory:
+// 4 stages (3 with fp32 output) at BN=256, 6 (5) at BN=128.
+template <typename TO, int BN> struct EpiCfg {
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr int kRing = BN == 256 ? (sizeof(TO) == 4 ? 3 : 4) : (sizeof(TO) == 4 ? 5 : 6);
   static constexpr uint32_t kOutBytes = 32 * 32 * sizeof(TO);
-  static constexpr uint32_t kEpiSmem = 4 * 2 * kOutBytes + 2 * kBN * 4;
+  static constexpr uint32_t kEpiSmem = 4 * 2 * kOutBytes + 2 * BN * 4;
+  static_assert(kRing <= kMaxStages, "ring deeper than the barrier arrays");
 };
 
 struct __align__(8) GemmBarriers {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t done;
@@ -88,16 +94,27 @@ __device__ __forceinline__ void act_chunk(float (&f)[32], const uint32_t (&r)[32
   for (int j = 0; j < 32; ++j) f[j] = apply_act(fmaf(__uint_as_float(r[j]), alpha, bv[j]), ACT);
 }
 
-template <typename TO, bool B_MN, bool TF32>
+// Split-K (few output tiles, long K): tile index t covers (output tile
+// t / splits, K range t % splits); each K range holds kb_per_split K blocks.
+// A split's raw fp32 accumulator goes to rows [split * m_pad, ...) of the
+// workspace matrix that tmC then describes; gemm_splitk_reduce_kernel sums the
+// splits and applies the epilogue.
+template <typename TO, bool B_MN, bool TF32, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int use_tma_store,
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
                   int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok,
-                  unsigned long long wait_ns, int stall_producer) {
-  constexpr int kRing = EpiCfg<TO>::kRing;
-  constexpr uint32_t kStageOutBytes = EpiCfg<TO>::kOutBytes;
-  constexpr uint32_t kEpiSmem = EpiCfg<TO>::kEpiSmem;
+                  unsigned long long wait_ns, int stall_producer, int splits, int kb_per_split,
+                  int m_pad) {
+  using Cfg = EpiCfg<TO, BN>;
+  constexpr int kBN = BN;
+  constexpr int kRing = Cfg::kRing;
+  constexpr uint32_t kBBytes = Cfg::kBBytes;
+  constexpr uint32_t kStageBytes = Cfg::kStageBytes;
+  constexpr uint32_t kTmemCols = Cfg::kTmemCols;
+  constexpr uint32_t kStageOutBytes = Cfg::kOutBytes;
+  constexpr uint32_t kEpiSmem = Cfg::kEpiSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -108,10 +125,16 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
-  const int tiles = num_m * num_n;
+  const int tiles = num_m * num_n * splits;
   static_assert(!(TF32 && B_MN), "tf32 operands are K-major");
   constexpr int kKE = TF32 ? 32 : kBK;  // K elements per 128-byte swizzle row
-  const int nk = (K + kKE - 1) / kKE;
+  const int nk_all = (K + kKE - 1) / kKE;
+  // K blocks [kb_lo, kb_hi) of tile index t
+  auto k_range = [&](int t, int& kb_lo, int& kb_hi) {
+    const int sp = t % splits;
+    kb_lo = sp * kb_per_split;
+    kb_hi = min(nk_all, kb_lo + kb_per_split);
+  };
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -148,9 +171,10 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       // stall_producer (failure-path test only): issue no loads, so the MMA
       // warp's first wait on a full stage runs out after wait_ns.
       for (int t = blockIdx.x; t < tiles && ok && !stall_producer; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < nk; ++kb) {
+        int mb, nb, kb_lo, kb_hi;
+        tile_coords(t / splits, num_m, num_n, mb, nb);
+        k_range(t, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, &g_gemm_status, DEV_TIMEOUT_SLOT, wait_ns)) {
             ok = false;
             break;
@@ -205,7 +229,9 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
-        for (int kb = 0; kb < nk; ++kb) {
+        int kb_lo, kb_hi;
+        k_range(t, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_TMA, wait_ns)) {
             ok = false;
             break;
@@ -220,8 +246,9 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                                      : sdesc(b0 + k * 32, 16, 1024, kSwizzle128);
             // 32 bytes of K per instruction: K=16 (f16/bf16) or K=8 (tf32)
             if (leader) {
-              if (TF32) mma_tf32_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-              else mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              const uint32_t accum = (kb != kb_lo || k != 0) ? 1u : 0u;
+              if (TF32) mma_tf32_ss(d_tmem, ad, bd, idesc, accum);
+              else mma_f16_ss(d_tmem, ad, bd, idesc, accum);
             }
           }
           issued = true;
@@ -258,7 +285,8 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     int tile_iter = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t / splits, num_m, num_n, mb, nb);
+      const int row_off = (t % splits) * m_pad;  // split-K: this split's rows of the workspace
       // This tile's bias columns into shared memory (double-buffered by tile
       // parity), loaded while the accumulator is still being computed.
       float* tb_bias = sBias + (tile_iter & 1) * kBN;
@@ -366,7 +394,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(stg, &tmC, n0, mb * kBM + quarter * 32);
+            tma_store_2d(stg, &tmC, n0, row_off + mb * kBM + quarter * 32);
             bulk_commit_group();
           }
           continue;
@@ -467,20 +495,112 @@ tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long 
   }
 }
 
-template <typename TO, bool B_MN, bool TF32 = false>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
-           const void* bias, int bias_dt, void* C,
-           long long M, long long N, long long K, long long ldc, float alpha, int act,
-           uint32_t idesc, int vec_ok, cudaStream_t st,
-           unsigned long long wait_ns = kWaitLimitNs, int stall_producer = 0) {
-  auto kern = gemm_sm100_kernel<TO, B_MN, TF32>;
-  const size_t smem = 1024 + EpiCfg<TO>::kRing * kStageBytes + EpiCfg<TO>::kEpiSmem + sizeof(GemmBarriers);
+// Launch parameters beyond the operands: tile width, split-K layout and the
+// failure-path test knobs.
+struct LaunchOpts {
+  int bn = 256;
+  int splits = 1, kb_per_split = 0, m_pad = 0;
+  unsigned long long wait_ns = kWaitLimitNs;
+  int stall_producer = 0;
+};
+
+template <typename TO, bool B_MN, bool TF32, int BN>
+int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
+              const void* bias, int bias_dt, void* C, long long M, long long N, long long K,
+              long long ldc, float alpha, int act, uint32_t idesc, int vec_ok, cudaStream_t st,
+              const LaunchOpts& o) {
+  using Cfg = EpiCfg<TO, BN>;
+  auto kern = gemm_sm100_kernel<TO, B_MN, TF32, BN>;
+  const size_t smem = 1024 + Cfg::kRing * Cfg::kStageBytes + Cfg::kEpiSmem + sizeof(GemmBarriers);
+  static_assert(1024 + Cfg::kRing * Cfg::kStageBytes + Cfg::kEpiSmem + sizeof(GemmBarriers) <= 227 * 1024,
+                "shared memory per CTA exceeded");
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int sms = device_sm_count();
-  const long long tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const long long tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * o.splits;
   const int grid = (int)(tiles < sms ? tiles : sms);
+  const int kbs = o.splits > 1 ? o.kb_per_split : (int)((K + 31) / 32);  // >= every K-block count
   kern<<<grid, kThreads, smem, st>>>(ta, tb, tc, use_tma, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
-                                      alpha, act, idesc, vec_ok, wait_ns, stall_producer);
+                                      alpha, act, idesc, vec_ok, o.wait_ns, o.stall_producer, o.splits,
+                                      kbs, o.m_pad);
+  B2_CHECK_LAUNCH();
+  return B2_OK;
+}
+
+template <typename TO, bool B_MN, bool TF32 = false>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, int use_tma,
+           const void* bias, int bias_dt, void* C, long long M, long long N, long long K,
+           long long ldc, float alpha, int act, uint32_t idesc, int vec_ok, cudaStream_t st,
+           const LaunchOpts& o = LaunchOpts()) {
+  if constexpr (!TF32) {
+    if (o.bn == 128)
+      return launch_bn<TO, B_MN, TF32, 128>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, ldc, alpha, act,
+                                            idesc, vec_ok, st, o);
+  }
+  return launch_bn<TO, B_MN, TF32, 256>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, ldc, alpha, act,
+                                        idesc, vec_ok, st, o);
+}
+
+}  // namespace
+
+struct GemmPlan {
+  int bn = 256;
+  int splits = 1, kb_per_split = 0;
+  long long m_pad = 0, np = 0;
+  size_t ws = 0;
+};
+
+namespace {
+
+// Split-K epilogue: C[m, n] = act(alpha * sum_s W[s * m_pad + m, n] + bias[n]),
+// four columns per thread (W's row pitch np is a multiple of 4 floats), the
+// splits summed in order (deterministic).
+template <typename TO, int ACT>
+__global__ void __launch_bounds__(256)
+gemm_splitk_reduce_kernel(const float* __restrict__ W, int splits, long long m_pad, long long np,
+                          const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, long long ldc,
+                          int M, int N, float alpha) {
+  const long long n4 = (N + 3) / 4;
+  const long long total = (long long)M * n4;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / n4;
+    const int n = (int)(i % n4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 w = *reinterpret_cast<const float4*>(W + ((long long)sp * m_pad + m) * np + n);
+      acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+    }
+    const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+    TO* crow = C + m * ldc;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (n + e >= N) break;
+      const float bv = bias ? bias_at(bias, bias_dt, n + e) : 0.f;
+      crow[n + e] = from_f32<TO>(apply_act(fmaf(a[e], alpha, bv), ACT));
+    }
+  }
+}
+
+template <typename TO>
+int splitk_reduce(const float* W, int splits, long long m_pad, long long np, const void* bias, int bias_dt,
+                  void* C, long long ldc, long long M, long long N, float alpha, int act, cudaStream_t st) {
+  const long long total = M * ((N + 3) / 4);
+  long long blocks = (total + 255) / 256;
+  const long long cap = (long long)device_sm_count() * 16;
+  if (blocks > cap) blocks = cap;
+  TO* c = reinterpret_cast<TO*>(C);
+  switch (act) {
+#define B2_SPLITK_CASE(A) \
+  case A: gemm_splitk_reduce_kernel<TO, A><<<(unsigned)blocks, 256, 0, st>>>(W, splits, m_pad, np, bias, bias_dt, c, ldc, (int)M, (int)N, alpha); break;
+    B2_SPLITK_CASE(B2_ACT_RELU)
+    B2_SPLITK_CASE(B2_ACT_GELU)
+    B2_SPLITK_CASE(B2_ACT_GELU_TANH)
+    B2_SPLITK_CASE(B2_ACT_SILU)
+    default:
+      gemm_splitk_reduce_kernel<TO, B2_ACT_NONE><<<(unsigned)blocks, 256, 0, st>>>(W, splits, m_pad, np, bias,
+                                                                                 bias_dt, c, ldc, (int)M, (int)N, alpha);
+#undef B2_SPLITK_CASE
+  }
   B2_CHECK_LAUNCH();
   return B2_OK;
 }
@@ -503,11 +623,65 @@ bool gemm_sm100_eligible(const void* A, const void* B, long long M, long long N,
   return false;
 }
 
+// Tile width and split-K choice for an fp16/bf16 GEMM (the reference's tile
+// choice with its occupancy gate, triton_msl/autotuning/matmul_tuner.py:76-104,
+// restated for a persistent kernel on the SM count):
+//  * BN = 128 instead of 256 when ceil(tiles / SMs) * BN is smaller (the last
+//    wave of 256-wide tiles would leave more SMs idle);
+//  * split-K when even 128-wide tiles fill at most half the SMs and K has at
+//    least 8 blocks of 64: the K blocks are divided into up to 32 ranges of at
+//    least 4 blocks, one CTA per (tile, range), partial sums in the workspace,
+//    and a reduce kernel applies alpha, bias and the activation. Not for the
+//    row-softmax epilogue (it needs whole rows in one tile).
+GemmPlan gemm_plan(long long M, long long N, long long K, int act) {
+  GemmPlan p;
+  if (M <= 0 || N <= 0 || K <= 0) return p;
+  const long long sms = device_sm_count();
+  auto tiles = [&](long long bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); };
+  auto cost = [&](long long bn) { return ((tiles(bn) + sms - 1) / sms) * bn; };
+  if (act == B2_ACT_SOFTMAX) return p;  // whole rows (N <= 256) in one 256-wide tile
+  if (cost(128) < cost(256)) p.bn = 128;
+  const long long nk = (K + kBK - 1) / kBK;
+  const long long t128 = tiles(128);
+  if (act != B2_ACT_SOFTMAX && 2 * t128 <= sms && nk >= 8) {
+    long long sp = sms / t128;
+    if (sp > nk / 4) sp = nk / 4;
+    if (sp > 32) sp = 32;
+    if (sp >= 2) {
+      const long long kbs = (nk + sp - 1) / sp;
+      p.bn = 128;
+      p.splits = (int)((nk + kbs - 1) / kbs);
+      p.kb_per_split = (int)kbs;
+      p.m_pad = (M + kBM - 1) / kBM * kBM;
+      p.np = (N + 3) / 4 * 4;
+      p.ws = (size_t)p.splits * (size_t)p.m_pad * (size_t)p.np * sizeof(float);
+    }
+  }
+  return p;
+}
+
 int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, long long M,
                       long long N, long long K, const int64_t* s, float alpha, int act, int in_dt,
-                      int bias_dt, int out_dt, cudaStream_t st) {
+                      int bias_dt, int out_dt, void* workspace, size_t ws_bytes, cudaStream_t st,
+                      int* variant) {
   const CUtensorMapDataType tdt =
       in_dt == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (s[5] != 1) {
+    set_error("b2_gemm: tensor-core path needs unit column stride in C");
+    return B2_EUNSUPPORTED;
+  }
+  GemmPlan plan = gemm_plan(M, N, K, act);
+  const bool split = plan.splits > 1 && workspace != nullptr && ws_bytes >= plan.ws &&
+                     (reinterpret_cast<uintptr_t>(workspace) & 15) == 0 && plan.m_pad * plan.splits < (1LL << 31);
+  LaunchOpts o;
+  o.bn = plan.bn;
+  if (split) {
+    o.splits = plan.splits;
+    o.kb_per_split = plan.kb_per_split;
+    o.m_pad = (int)plan.m_pad;
+  }
+  const int BN = o.bn;
+  if (variant) *variant = split ? 2 : (BN == 128 ? 1 : 0);
   CUtensorMap ta, tb;
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
@@ -524,17 +698,34 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
   } else {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)s[3] * 2};
-    const uint32_t box[2] = {kBK, kBN};
+    const uint32_t box[2] = {kBK, (uint32_t)BN};
     if (!encode_tmap(&tb, tdt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
   }
-  const uint32_t idesc = idesc_f16(kBM, kBN, in_dt == B2_BF16, false, b_mn);
-  const int osz = dtype_size(out_dt);
-  const int vec_ok = s[5] == 1 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
-  if (s[5] != 1) {
-    set_error("b2_gemm: tensor-core path needs unit column stride in C");
-    return B2_EUNSUPPORTED;
-  }
+  const uint32_t idesc = idesc_f16(kBM, BN, in_dt == B2_BF16, false, b_mn);
   if (bias == nullptr) bias_dt = B2_F32;
+  if (split) {
+    // partial sums: fp32 [splits * m_pad, N] (row pitch np) through TMA stores
+    CUtensorMap tw;
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)(plan.splits * plan.m_pad)};
+    const uint64_t strides[1] = {(uint64_t)plan.np * 4};
+    const uint32_t box[2] = {32, 32};
+    if (!encode_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, workspace, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+    int rc = b_mn ? launch<float, true>(ta, tb, tw, 1, nullptr, B2_F32, workspace, M, N, K, plan.np, 1.f,
+                                        B2_ACT_NONE, idesc, 1, st, o)
+                  : launch<float, false>(ta, tb, tw, 1, nullptr, B2_F32, workspace, M, N, K, plan.np, 1.f,
+                                         B2_ACT_NONE, idesc, 1, st, o);
+    if (rc != B2_OK) return rc;
+    const float* W = reinterpret_cast<const float*>(workspace);
+    switch (out_dt) {
+      case B2_F16: return splitk_reduce<__half>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+      case B2_BF16: return splitk_reduce<__nv_bfloat16>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+      default: return splitk_reduce<float>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+    }
+  }
+  const int osz = dtype_size(out_dt);
+  const int vec_ok = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
   // Output through TMA tensor stores when C's base and row pitch allow it.
   CUtensorMap tc;
   int use_tma = 0;
@@ -552,17 +743,25 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
   if (!use_tma) memset(&tc, 0, sizeof(tc));
   switch (out_dt) {
     case B2_F16:
-      return b_mn ? launch<__half, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<__half, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<__half, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o)
+                  : launch<__half, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o);
     case B2_BF16:
-      return b_mn ? launch<__nv_bfloat16, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<__nv_bfloat16, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<__nv_bfloat16, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o)
+                  : launch<__nv_bfloat16, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o);
     case B2_F32:
-      return b_mn ? launch<float, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st)
-                  : launch<float, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st);
+      return b_mn ? launch<float, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o)
+                  : launch<float, false>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K, s[4], alpha, act, idesc, vec_ok, st, o);
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;
+}
+
+size_t gemm_f16_workspace(long long M, long long N, long long K, int act) {
+  return gemm_plan(M, N, K, act).ws;
+}
+
+int gemm_f16_plan_splits(long long M, long long N, long long K, int act) {
+  return gemm_plan(M, N, K, act).splits;
 }
 
 size_t gemm_tf32x3_workspace(long long M, long long N, long long K) {
@@ -606,11 +805,11 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
   {
     const uint64_t dims[2] = {(uint64_t)K3, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K3 * 4};
-    const uint32_t box[2] = {32, kBN};
+    const uint32_t box[2] = {32, 256};
     if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Bp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return B2_ELAUNCH;
   }
-  const uint32_t idesc = idesc_tf32(kBM, kBN);
+  const uint32_t idesc = idesc_tf32(kBM, 256);
   const int osz = dtype_size(out_dt);
   const int vec_ok = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
   if (bias == nullptr) bias_dt = B2_F32;
@@ -658,14 +857,17 @@ int gemm_stall_test_launch(const void* A, const void* B, void* C, long long M, l
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {kBK, kBN};
+    const uint32_t box[2] = {kBK, 256};
     if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return B2_ELAUNCH;
   }
   memset(&tc, 0, sizeof(tc));
-  const uint32_t idesc = idesc_f16(kBM, kBN, false, false, false);
+  const uint32_t idesc = idesc_f16(kBM, 256, false, false, false);
+  LaunchOpts o;
+  o.wait_ns = wait_ns;
+  o.stall_producer = 1;
   return launch<__half, false>(ta, tb, tc, 0, nullptr, B2_F32, C, M, N, K, N, 1.f, B2_ACT_NONE, idesc,
-                               0, st, wait_ns, 1);
+                               0, st, o);
 }
 
 uint32_t gemm_read_status(bool clear) {

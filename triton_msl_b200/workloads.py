@@ -72,6 +72,8 @@ FA_F16_CAUSAL_D64 = FAConfig("fa_f16_causal_B4_H16_S2048_D64", 4, 16, 2048, 64, 
                              torch.float16, 0.5)
 FA_F16_CAUSAL_D32 = FAConfig("fa_f16_causal_B4_H16_S2048_D32", 4, 16, 2048, 32, True,
                              torch.float16, 0.5)
+FA_BF16_CAUSAL = FAConfig("fa_bf16_causal_B4_H16_S2048_D128", 4, 16, 2048, 128, True,
+                          torch.bfloat16, 0.5)
 FA_BF16_SCALE = FAConfig("fa_bf16_causal_B64_H32_S8192_D128", 64, 32, 8192, 128, True,
                          torch.bfloat16, 0.5)
 GEMM_F16 = GemmConfig("gemm_f16_8192_bias_relu", 8192, 8192, 8192, torch.float16, True, "relu",
