@@ -113,8 +113,7 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o,
  * alone; the tensor core's fp32 accumulation adds an error that grows with K,
  * measured 2.5e-5 * max|C| at K=2048); with no workspace, fp32 FMA.
  * fp16/bf16 inputs: the tile width (128x256 or 128x128) follows the SM count
- * (the narrower tile when the last wave of wide tiles would leave more SMs
- * idle); when even narrow tiles would fill at most half the SMs and K >= 512,
+ * (the narrower tile when wide tiles would not fill every SM once); when even narrow tiles would fill at most half the SMs and K >= 512,
  * the K loop is split across CTAs (split-K) given the workspace
  * b2_query_workspace reports, with fp32 partial sums reduced in a fixed order
  * before the epilogue (without the workspace the unsplit kernel runs).

@@ -143,21 +143,52 @@ def test_gemm_epilogue(act, out_dtype):
 # tiles with a long K split the K loop across CTAs; shapes whose last wave of
 # 128x256 tiles would idle more SMs take 128x128 tiles.
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("M,N,K,variant", [
-    (256, 256, 8192, "gemm_sm100_splitk"),
-    (100, 300, 5000, "gemm_sm100_splitk"),     # ragged M, N; uneven K ranges
-    (64, 1001, 2048, "gemm_sm100_splitk"),     # N not a multiple of 4
-    (1024, 1024, 4096, "gemm_sm100_splitk"),
-    (4096, 4096, 512, "gemm_sm100_n128"),
-    (2000, 3000, 320, "gemm_sm100_n128"),
-    (512, 512, 256, "gemm_sm100_n128"),        # K too short to split
+@pytest.mark.parametrize("M,N,K,b_kmajor,variant", [
+    (256, 256, 8192, False, "gemm_sm100_splitk"),
+    (100, 296, 5008, False, "gemm_sm100_splitk"),   # ragged M, N; uneven K ranges
+    (64, 1001, 2048, True, "gemm_sm100_splitk"),    # N not a multiple of 4 (K-major B)
+    (1024, 1024, 4096, False, "gemm_sm100_splitk"),
+    (512, 4096, 4096, False, "gemm_sm100_n128"),    # < 1 wave of 128x256 tiles
+    (1000, 1500, 320, True, "gemm_sm100_n128"),
+    (512, 512, 256, False, "gemm_sm100_n128"),      # K too short to split
+    (4096, 4096, 512, False, "gemm_sm100_pair"),
 ])
-def test_gemm_tile_choice_paths(dtype, M, N, K, variant):
+def test_gemm_tile_choice_paths(dtype, M, N, K, b_kmajor, variant):
     a = _rand((M, K), dtype, 61, 1 / math.sqrt(K))
-    b = _rand((K, N), dtype, 62, 1 / math.sqrt(K))
-    c = b2.gemm(a.to(DEV), b.to(DEV))
+    if b_kmajor:
+        w = _rand((N, K), dtype, 62, 1 / math.sqrt(K))
+        b = w.t()
+        c = b2.gemm(a.to(DEV), w.to(DEV).t())
+    else:
+        b = _rand((K, N), dtype, 62, 1 / math.sqrt(K))
+        c = b2.gemm(a.to(DEV), b.to(DEV))
     assert b2.last_kernel() == variant
     _check(c, O.ref_gemm(a, b, out_dtype=torch.float32), dtype)
+
+
+# Shapes with a full wave of 256x256 tiles run on CTA pairs (tcgen05
+# cta_group::2, M=256 MMAs): ragged M/N/K, both B layouts, epilogues, outputs.
+@pytest.mark.parametrize("M,N,K,b_kmajor,act,out_dtype,dtype", [
+    (2000, 2504, 1000, False, "relu", torch.float16, torch.float16),
+    (2000, 2504, 1000, True, "gelu", torch.bfloat16, torch.bfloat16),
+    (2304, 2304, 2048, False, "none", torch.float32, torch.bfloat16),
+    (2304, 2304, 2048, True, "silu", torch.float32, torch.float16),
+    (4100, 2056, 520, True, "gelu_tanh", torch.float16, torch.float16),
+])
+def test_gemm_pair_paths(M, N, K, b_kmajor, act, out_dtype, dtype):
+    a = _rand((M, K), dtype, 91, 1 / math.sqrt(K))
+    bias = _rand((N,), torch.float32, 93, 0.1)
+    if b_kmajor:
+        w = _rand((N, K), dtype, 92, 1 / math.sqrt(K))
+        b, bd = w.t(), w.to(DEV).t()
+    else:
+        b = _rand((K, N), dtype, 92, 1 / math.sqrt(K))
+        bd = b.to(DEV)
+    c = b2.gemm(a.to(DEV), bd, bias.to(DEV), act, out_dtype, alpha=1.25)
+    assert b2.last_kernel() == "gemm_sm100_pair"
+    assert c.dtype == out_dtype
+    _check(c, O.ref_gemm(a, b, bias, act, torch.float32, alpha=1.25), dtype)
+    assert b2.device_status(0) == 0
 
 
 @pytest.mark.parametrize("act", ["none", "relu", "gelu", "silu"])

@@ -34,6 +34,7 @@ int gemm_stall_test_launch(const void*, const void*, void*, long long, long long
                            unsigned long long, cudaStream_t);
 uint32_t row_read_status(bool);
 uint32_t gemm_read_status(bool);
+uint32_t pair_read_status(bool);
 uint32_t fa_read_status(bool);
 
 namespace {
@@ -201,7 +202,10 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
     rc = gemm_sm100_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
                            out_dtype, workspace, ws_bytes, st, &variant);
     if (rc == B2_OK)
-      t_kernel = variant == 2 ? "gemm_sm100_splitk" : variant == 1 ? "gemm_sm100_n128" : "gemm_sm100";
+      t_kernel = variant == 3   ? "gemm_sm100_pair"
+                 : variant == 2 ? "gemm_sm100_splitk"
+                 : variant == 1 ? "gemm_sm100_n128"
+                                : "gemm_sm100";
   } else {
     rc = gemm_simt_launch(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype,
                           out_dtype, st);
@@ -308,6 +312,7 @@ int b2_device_status(int device, int clear, uint32_t* status_out) {
   if (e == cudaSuccess) {
     s |= row_read_status(clear != 0);
     s |= gemm_read_status(clear != 0);
+    s |= pair_read_status(clear != 0);
     s |= fa_read_status(clear != 0);
     e = cudaGetLastError();
   }

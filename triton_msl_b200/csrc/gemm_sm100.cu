@@ -21,6 +21,7 @@
 //  * Epilogue: tcgen05.ld 32 columns at a time, alpha, + bias[n], activation,
 //    convert, 16-byte stores.
 //  * Every mbarrier wait is bounded (see sm100.cuh).
+#include <cstdlib>
 #include <cstring>
 
 #include "sm100.cuh"
@@ -299,9 +300,10 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
       ++tile_iter;
-      // (in the stall test the MMA warp's shorter wait gives up first)
+      // In the stall test only the MMA warp's wait is shortened; this one keeps
+      // the full limit and leaves on the abort flag the MMA warp sets.
       if (!mbar_wait(&bars->acc_full[acc], acc_phase, abort_flag, &g_gemm_status, DEV_TIMEOUT_MMA,
-                     stall_producer ? 4 * wait_ns : wait_ns))
+                     stall_producer ? kWaitLimitNs : wait_ns))
         break;
       tc_fence_after();
       const int row = mb * kBM + quarter * 32 + lane;
@@ -626,25 +628,52 @@ bool gemm_sm100_eligible(const void* A, const void* B, long long M, long long N,
 // Tile width and split-K choice for an fp16/bf16 GEMM (the reference's tile
 // choice with its occupancy gate, triton_msl/autotuning/matmul_tuner.py:76-104,
 // restated for a persistent kernel on the SM count):
-//  * BN = 128 instead of 256 when ceil(tiles / SMs) * BN is smaller (the last
-//    wave of 256-wide tiles would leave more SMs idle);
+//  * BN = 128 instead of 256 when 128x256 tiles would not fill the SMs once
+//    (measured on B200: the narrow tile moves 33 % more operand bytes per
+//    MMA cycle and loses 15-30 % at full occupancy, so it only pays when it
+//    turns idle SMs into busy ones);
 //  * split-K when even 128-wide tiles fill at most half the SMs and K has at
 //    least 8 blocks of 64: the K blocks are divided into up to 32 ranges of at
 //    least 4 blocks, one CTA per (tile, range), partial sums in the workspace,
 //    and a reduce kernel applies alpha, bias and the activation. Not for the
 //    row-softmax epilogue (it needs whole rows in one tile).
+// B2MSL_GEMM_TILE=256|128|splitk|pair (read once) forces a tile choice where it
+// applies: a tuning and diagnostic override, unset in normal use.
+int tile_override() {
+  static const int v = [] {
+    const char* e = getenv("B2MSL_GEMM_TILE");
+    if (!e) return 0;
+    if (!strcmp(e, "256")) return 256;
+    if (!strcmp(e, "128")) return 128;
+    if (!strcmp(e, "splitk")) return 1;
+    if (!strcmp(e, "pair")) return 2;
+    return 0;
+  }();
+  return v;
+}
+
+bool gemm_pair_wanted(long long M, long long N, long long K, const int64_t* s, const void* C, int out_dt,
+                      int act, bool forced);
+int gemm_pair_launch(const void* A, const void* B, const void* bias, void* C, long long M, long long N,
+                     long long K, const int64_t* s, float alpha, int act, int in_dt, int bias_dt, int out_dt,
+                     cudaStream_t st);
+
 GemmPlan gemm_plan(long long M, long long N, long long K, int act) {
   GemmPlan p;
   if (M <= 0 || N <= 0 || K <= 0) return p;
+  const int force = tile_override();
+  if (force == 256 || force == 2 || (force == 128 && act != B2_ACT_SOFTMAX)) {
+    p.bn = force == 128 ? 128 : 256;
+    return p;
+  }
   const long long sms = device_sm_count();
   auto tiles = [&](long long bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); };
-  auto cost = [&](long long bn) { return ((tiles(bn) + sms - 1) / sms) * bn; };
   if (act == B2_ACT_SOFTMAX) return p;  // whole rows (N <= 256) in one 256-wide tile
-  if (cost(128) < cost(256)) p.bn = 128;
+  if (tiles(256) < sms) p.bn = 128;  // less than one wave of wide tiles
   const long long nk = (K + kBK - 1) / kBK;
   const long long t128 = tiles(128);
-  if (act != B2_ACT_SOFTMAX && 2 * t128 <= sms && nk >= 8) {
-    long long sp = sms / t128;
+  if (act != B2_ACT_SOFTMAX && ((2 * t128 <= sms && nk >= 8) || (force == 1 && nk >= 8))) {
+    long long sp = force == 1 ? (sms + t128 - 1) / t128 : sms / t128;
     if (sp > nk / 4) sp = nk / 4;
     if (sp > 32) sp = 32;
     if (sp >= 2) {
@@ -681,6 +710,11 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
     o.m_pad = (int)plan.m_pad;
   }
   const int BN = o.bn;
+  if (!split && BN == 256 && tile_override() != 256 &&
+      gemm_pair_wanted(M, N, K, s, C, out_dt, act, tile_override() == 2)) {
+    if (variant) *variant = 3;
+    return gemm_pair_launch(A, B, bias, C, M, N, K, s, alpha, act, in_dt, bias_dt, out_dt, st);
+  }
   if (variant) *variant = split ? 2 : (BN == 128 ? 1 : 0);
   CUtensorMap ta, tb;
   {
