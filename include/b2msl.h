@@ -73,7 +73,7 @@ const char* b2_last_error(void);
 
 /* Kernel family the calling thread's last successful call launched
  * ("fa_sm100", "fa_simt", "gemm_sm100" (128x256 tiles), "gemm_sm100_n128"
- * (128x128 tiles), "gemm_sm100_splitk", "gemm_sm100_tf32x3", "gemm_simt",
+ * (128x128 tiles), "gemm_sm100_pair" (256x256 tiles on CTA pairs), "gemm_sm100_splitk", "gemm_sm100_tf32x3", "gemm_simt",
  * "row_reduce", "row_split", "row_memset"). Introspection for tests and benchmarks; the reference's
  * equivalent is its TRITON_MSL_PATH_LOG lowering-path log
  * (triton_msl/codegen/msl_emitter.py:523-538). */
@@ -112,8 +112,10 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o,
  * (x = hi + lo, A.B = hi.hi + hi.lo + lo.hi; no input rounding to TF32
  * alone; the tensor core's fp32 accumulation adds an error that grows with K,
  * measured 2.5e-5 * max|C| at K=2048); with no workspace, fp32 FMA.
- * fp16/bf16 inputs: the tile width (128x256 or 128x128) follows the SM count
- * (the narrower tile when wide tiles would not fill every SM once); when even narrow tiles would fill at most half the SMs and K >= 512,
+ * fp16/bf16 inputs: shapes with at least one full wave of 256x256 output
+ * tiles run on CTA pairs (two SMs per tile, M=256 tensor-core MMAs); smaller
+ * ones on one SM per 128x256 or 128x128 tile, whichever leaves fewer SMs
+ * idle for the work; when even narrow tiles would fill at most half the SMs and K >= 512,
  * the K loop is split across CTAs (split-K) given the workspace
  * b2_query_workspace reports, with fp32 partial sums reduced in a fixed order
  * before the epilogue (without the workspace the unsplit kernel runs).

@@ -628,10 +628,11 @@ bool gemm_sm100_eligible(const void* A, const void* B, long long M, long long N,
 // Tile width and split-K choice for an fp16/bf16 GEMM (the reference's tile
 // choice with its occupancy gate, triton_msl/autotuning/matmul_tuner.py:76-104,
 // restated for a persistent kernel on the SM count):
-//  * BN = 128 instead of 256 when 128x256 tiles would not fill the SMs once
-//    (measured on B200: the narrow tile moves 33 % more operand bytes per
-//    MMA cycle and loses 15-30 % at full occupancy, so it only pays when it
-//    turns idle SMs into busy ones);
+//  * BN = 128 instead of 256 when ceil(tiles / SMs) x tile cost is lower,
+//    with a 128-wide tile costing 1.25x half a wide one (measured on B200: the
+//    narrow tile moves 33 % more operand bytes per MMA cycle and loses
+//    15-30 % at full occupancy, so it only pays when it turns idle SMs into
+//    busy ones, e.g. 512 x 4096 but not 2048 x 2048);
 //  * split-K when even 128-wide tiles fill at most half the SMs and K has at
 //    least 8 blocks of 64: the K blocks are divided into up to 32 ranges of at
 //    least 4 blocks, one CTA per (tile, range), partial sums in the workspace,
@@ -669,7 +670,10 @@ GemmPlan gemm_plan(long long M, long long N, long long K, int act) {
   const long long sms = device_sm_count();
   auto tiles = [&](long long bn) { return ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn); };
   if (act == B2_ACT_SOFTMAX) return p;  // whole rows (N <= 256) in one 256-wide tile
-  if (tiles(256) < sms) p.bn = 128;  // less than one wave of wide tiles
+  // waves x tile width, the narrow tile weighted by its measured 1.25x cost
+  // per output column
+  auto cost = [&](long long bn) { return ((tiles(bn) + sms - 1) / sms) * (bn == 128 ? 160 : 256); };
+  if (cost(128) < cost(256)) p.bn = 128;
   const long long nk = (K + kBK - 1) / kBK;
   const long long t128 = tiles(128);
   if (act != B2_ACT_SOFTMAX && ((2 * t128 <= sms && nk >= 8) || (force == 1 && nk >= 8))) {
@@ -710,7 +714,7 @@ int gemm_sm100_launch(const void* A, const void* B, const void* bias, void* C, l
     o.m_pad = (int)plan.m_pad;
   }
   const int BN = o.bn;
-  if (!split && BN == 256 && tile_override() != 256 &&
+  if (!split && tile_override() != 256 && tile_override() != 128 &&
       gemm_pair_wanted(M, N, K, s, C, out_dt, act, tile_override() == 2)) {
     if (variant) *variant = 3;
     return gemm_pair_launch(A, B, bias, C, M, N, K, s, alpha, act, in_dt, bias_dt, out_dt, st);
