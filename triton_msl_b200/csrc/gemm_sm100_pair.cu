@@ -3,7 +3,7 @@
 // Same contract as gemm_sm100.cu (C = act(alpha * A.B + bias), fp32
 // accumulate; the reference's fast matmul, triton_msl/codegen/_msl_templates.py:4134-4255,
 // with the epilogue of _lowerer_templates.py:1515-1855), for shapes with at
-// least one full wave of output tiles. Two CTAs on two SMs (a cluster of 2)
+// least one full wave of output tiles and at most 4e12 FLOP. Two CTAs on two SMs (a cluster of 2)
 // compute one 256 x 256 output tile with M=256 MMAs issued by rank 0:
 //  * each CTA loads its own 128 rows of A and its own 128 columns of B (K step
 //    64) into its own shared memory; the pair's tensor cores share the B
@@ -38,7 +38,7 @@ constexpr uint32_t kBBytes = kHalf * kBK * 2;  // 16 KB: this CTA's B columns
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 2 * kBN;
 #ifndef B2_GEMM_PAIR_GROUP_M
-#define B2_GEMM_PAIR_GROUP_M 8
+#define B2_GEMM_PAIR_GROUP_M 16
 #endif
 constexpr int kGroupM = B2_GEMM_PAIR_GROUP_M;  // raster: 256-row blocks per group
 
@@ -351,7 +351,8 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 
 // True when the pair kernel serves this call: fp16/bf16 in, no row-softmax
 // epilogue, C describable by a TMA map (16-byte aligned base and row pitch,
-// unit column stride), and at least one full wave of 256 x 256 tiles.
+// unit column stride), at least one full wave of 256 x 256 tiles, and a
+// problem short enough to run at burst clocks (<= 4e12 FLOP).
 bool gemm_pair_wanted(long long M, long long N, long long K, const int64_t* s, const void* C, int out_dt,
                       int act, bool forced) {
   if (act == B2_ACT_SOFTMAX || K <= 0) return false;
@@ -359,7 +360,11 @@ bool gemm_pair_wanted(long long M, long long N, long long K, const int64_t* s, c
   if (s[5] != 1 || (reinterpret_cast<uintptr_t>(C) & 15) != 0 || (s[4] * osz) % 16 != 0 || s[4] < N) return false;
   if (forced) return true;
   const long long tiles = ((M + kPM - 1) / kPM) * ((N + kBN - 1) / kBN);
-  return 2 * tiles >= device_sm_count();
+  // Measured on B200 (bf16, L2 flushed): pairs win 7-12 % at 4096^3..8192^3
+  // (1300 / 1590 vs 1150 / 1475 TFLOP/s), but on a 35-TFLOP problem that runs
+  // tens of ms under the 1 kW power cap the one-SM kernel sustained
+  // 1220 vs 1050-1180; pairs are used up to 4e12 FLOP per call.
+  return 2 * tiles >= device_sm_count() && 2.0 * (double)M * (double)N * (double)K <= 4e12;
 }
 
 int gemm_pair_launch(const void* A, const void* B, const void* bias, void* C, long long M, long long N,
