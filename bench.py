@@ -429,16 +429,15 @@ def run_b2(args, world, rank, local):
     kern = b2.last_kernel()
     if kern != "fa_sm100":
         raise RuntimeError(f"headline FA ran on {kern}, not the tensor-core kernel")
-    # Rank 0 samples the clocks of every GPU of the job from before the first
-    # timed step to the end of the GPU work (the headline's own timed region is
-    # a few milliseconds, shorter than one 200 ms sample). No extended pre-warm:
-    # the idle SM clock is already the maximum, and a sub-second loop of
-    # back-to-back launches before the timed steps tripped the power cap.
-    sampler = ClockSampler(",".join(str(i) for i in range(world)) if world > 1 else local) \
-        if rank == 0 else None
-    if sampler:
-        sampler.__enter__()
-        sampler.wait_first(5.0)
+    # Each rank samples its own GPU's clocks from before the first timed step to
+    # the end of the GPU work (the headline's own timed region is a few
+    # milliseconds, shorter than one 200 ms sample); rank 0 gathers the
+    # summaries. No extended pre-warm: the idle SM clock is already the maximum,
+    # and a sub-second loop of back-to-back launches before the timed steps
+    # tripped the power cap.
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    sampler.wait_first(5.0)
     try:
         times = time_launches(fa, args.steps, args.warmup, flush, world)
         ms_rank = statistics.mean(times)
@@ -462,15 +461,20 @@ def run_b2(args, world, rank, local):
         torch.cuda.synchronize()
         barrier(world)
         st = torch.cuda.current_stream()
-        a = torch.cuda.Event(enable_timing=True)
-        bev = torch.cuda.Event(enable_timing=True)
-        a.record(st)
-        for _ in range(args.steps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        h0 = time.perf_counter()
+        evs[0].record(st)
+        for i in range(args.steps):
             e2e_step()
-        bev.record(st)
+            evs[i + 1].record(st)
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         torch.cuda.synchronize()
         barrier(world)
-        e2e_per_rank = all_gather_floats(a.elapsed_time(bev) / args.steps, world)
+        step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+        e2e_per_rank = all_gather_floats(sum(step_ms) / args.steps, world)
+        e2e_host_ms = max(all_gather_floats(host_ms, world))
+        e2e_step_max = max(all_gather_floats(max(step_ms), world))
+        e2e_step_min = max(all_gather_floats(min(step_ms), world))
         e2e_ms = max(e2e_per_rank)
         e2e_val = world * flops / (e2e_ms / 1e3) / 1e12
         h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
@@ -478,6 +482,8 @@ def run_b2(args, world, rank, local):
         del hq, hk, hv, ho, q, k, v
         link = measure_link(h2d, d2h, dev, world)
         link["e2e_ms"] = round(e2e_ms, 4)
+        link["e2e_step_ms_min_max"] = [round(e2e_step_min, 4), round(e2e_step_max, 4)]
+        link["e2e_host_enqueue_ms_per_step"] = round(e2e_host_ms, 4)
         link["e2e_frac_of_link"] = round(link["both_ms"] / e2e_ms, 4)
         link["note"] = ("e2e is bounded by the host link: both_ms = the step's host->device and "
                         "device->host bytes as plain pinned copies, both directions at once, "
@@ -490,12 +496,23 @@ def run_b2(args, world, rank, local):
             extra.update(run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
                                    threads, model))
     finally:
-        if sampler:
-            sampler.__exit__()
+        sampler.__exit__()
 
+    summaries = [sampler.summary()]
+    if world > 1:
+        import torch.distributed as dist
+        summaries = [None] * world
+        dist.all_gather_object(summaries, sampler.summary())
     if rank != 0:
         return
-    clocks = sampler.summary() if sampler else None
+    clocks = summaries[0]
+    if world > 1:
+        mhz = [c["sm_mhz"] for c in summaries if c.get("sm_mhz")]
+        clocks = {"sm_mhz": statistics.median(mhz) if mhz else None,
+                  "sm_max_mhz": max((c["sm_max_mhz"] or 0) for c in summaries) or None,
+                  "reasons": sorted({r for c in summaries for r in c["reasons"]}),
+                  "samples": sum(c.get("samples", 0) for c in summaries),
+                  "sm_mhz_per_rank": [c["sm_mhz"] for c in summaries]}
     threads_all, _ = cpu_info()
     torch.set_num_threads(threads_all)
     cb = cpu_fa(cfg, args.cpu_seconds if world == 1 else 3.0, threads_all, model)
