@@ -90,9 +90,6 @@ struct FaCfg {
 #ifndef B2_FA_MUFU8_D128
 #define B2_FA_MUFU8_D128 5
 #endif
-#ifndef B2_FA_PCHUNK
-#define B2_FA_PCHUNK 0
-#endif
 #ifndef B2_FA_MUFU8_SMALL
 #define B2_FA_MUFU8_SMALL 4
 #endif
@@ -537,15 +534,6 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
         if constexpr (!Cfg::kSumMma) acc2[i & 3] = f2_add(acc2[i & 3], f2_pack(p0, p1));
         p[i] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
-#if B2_FA_PCHUNK
-        // hand each 32-key piece of P to TMEM as soon as it is packed
-        if ((i & 15) == 15) {
-          uint32_t r[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) r[e] = p[i - 15 + e];
-          tmem_st16(tS[t] + lane_off + (i - 15), r);
-        }
-#endif
       }
       if constexpr (!Cfg::kSumMma) {
         const f2_t a01 = f2_add(acc2[0], acc2[1]), a23 = f2_add(acc2[2], acc2[3]);
@@ -553,7 +541,6 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         f2_unpack(f2_add(a01, a23), u0, u1);
         l_run = l_run * alpha + (u0 + u1);
       }
-#if !B2_FA_PCHUNK
 #pragma unroll
       for (int c = 0; c < kBN / 2 / 32; ++c) {
         uint32_t r[32];
@@ -561,7 +548,6 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int i = 0; i < 32; ++i) r[i] = p[c * 32 + i];
         tmem_st32(tS[t] + lane_off + c * 32, r);
       }
-#endif
       if (warp_rescale && j > 0) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
