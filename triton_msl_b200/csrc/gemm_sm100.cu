@@ -802,10 +802,46 @@ int gemm_f16_plan_splits(long long M, long long N, long long K, int act) {
   return gemm_plan(M, N, K, act).splits;
 }
 
+// Split-K plan of the 3xTF32 GEMM (one 128x256 tile per CTA): when the tiles
+// fill at most half the SMs (2048^3 has 64 tiles), the tripled K loop is split
+// like the fp16 path's (gemm_plan) so every SM works; not with the row-softmax
+// epilogue.
+struct Tf32Plan {
+  int splits = 1, kb_per_split = 0;
+  long long m_pad = 0, np = 0;
+  size_t ws = 0;
+};
+
+Tf32Plan tf32_plan(long long M, long long N, long long K, int act) {
+  Tf32Plan p;
+  if (M <= 0 || N <= 0 || K <= 0 || act == B2_ACT_SOFTMAX) return p;
+  const long long sms = device_sm_count();
+  const long long tiles = ((M + kBM - 1) / kBM) * ((N + 255) / 256);
+  const long long nk = 3 * ((K + 31) / 32);  // 32-element K blocks over the tripled K
+  if (2 * tiles <= sms && nk >= 8) {
+    long long sp = sms / tiles;
+    if (sp > nk / 4) sp = nk / 4;
+    if (sp > 32) sp = 32;
+    if (sp >= 2) {
+      const long long kbs = (nk + sp - 1) / sp;
+      p.splits = (int)((nk + kbs - 1) / kbs);
+      p.kb_per_split = (int)kbs;
+      p.m_pad = (M + kBM - 1) / kBM * kBM;
+      p.np = (N + 3) / 4 * 4;
+      p.ws = (size_t)p.splits * (size_t)p.m_pad * (size_t)p.np * sizeof(float);
+    }
+  }
+  return p;
+}
+
+size_t tf32_operand_bytes(long long M, long long N, long long K) {
+  const long long Kp = (K + 31) / 32 * 32;
+  return ((size_t)(M + N) * 3 * (size_t)Kp * sizeof(float) + 255) / 256 * 256;
+}
+
 size_t gemm_tf32x3_workspace(long long M, long long N, long long K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const long long Kp = (K + 31) / 32 * 32;
-  return (size_t)(M + N) * 3 * (size_t)Kp * sizeof(float);
+  return tf32_operand_bytes(M, N, K) + tf32_plan(M, N, K, B2_ACT_NONE).ws;
 }
 
 int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C, long long M,
@@ -851,6 +887,28 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
   const int osz = dtype_size(out_dt);
   const int vec_ok = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && ((s[4] * osz) % 16) == 0;
   if (bias == nullptr) bias_dt = B2_F32;
+  const Tf32Plan plan = tf32_plan(M, N, K, act);
+  if (plan.splits > 1 && plan.m_pad * plan.splits < (1LL << 31)) {
+    float* W = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + tf32_operand_bytes(M, N, K));
+    CUtensorMap tw;
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)(plan.splits * plan.m_pad)};
+    const uint64_t strides[1] = {(uint64_t)plan.np * 4};
+    const uint32_t box[2] = {32, 32};
+    if (!encode_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, W, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return B2_ELAUNCH;
+    LaunchOpts o;
+    o.splits = plan.splits;
+    o.kb_per_split = plan.kb_per_split;
+    o.m_pad = (int)plan.m_pad;
+    const int rc = launch<float, false, true>(ta, tb, tw, 1, nullptr, B2_F32, W, M, N, K3, plan.np, 1.f,
+                                              B2_ACT_NONE, idesc, 1, st, o);
+    if (rc != B2_OK) return rc;
+    switch (out_dt) {
+      case B2_F16: return splitk_reduce<__half>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+      case B2_BF16: return splitk_reduce<__nv_bfloat16>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+      default: return splitk_reduce<float>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
+    }
+  }
   CUtensorMap tc;
   int use_tma = 0;
   if (vec_ok && s[4] >= N) {
