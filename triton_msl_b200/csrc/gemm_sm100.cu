@@ -107,7 +107,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
                   int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok,
                   unsigned long long wait_ns, int stall_producer, int splits, int kb_per_split,
-                  int m_pad) {
+                  int m_pad, int tf32_kp_blocks) {
   using Cfg = EpiCfg<TO, BN>;
   constexpr int kBN = BN;
   constexpr int kRing = Cfg::kRing;
@@ -181,14 +181,22 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             break;
           }
           mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
-          tma_load_2d(sA + stage * kABytes, &tmA, &bars->full[stage], kb * kKE, mb * kBM);
+          int xa = kb * kKE, xb = kb * kKE;
+          if constexpr (TF32) {
+            // tripled K = [hi.hi | hi.lo | lo.hi] over operands stored as [hi | lo]
+            const int seg = kb / tf32_kp_blocks, off = (kb - seg * tf32_kp_blocks) * kKE;
+            const int kp = tf32_kp_blocks * kKE;
+            xa = off + (seg == 2 ? kp : 0);
+            xb = off + (seg == 1 ? kp : 0);
+          }
+          tma_load_2d(sA + stage * kABytes, &tmA, &bars->full[stage], xa, mb * kBM);
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < kBN / 64; ++j)
               tma_load_2d(sB + stage * kBBytes + j * (64 * kBK * 2), &tmB, &bars->full[stage],
                           nb * kBN + j * 64, kb * kBK);
           } else {
-            tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], kb * kKE, nb * kBN);
+            tma_load_2d(sB + stage * kBBytes, &tmB, &bars->full[stage], xb, nb * kBN);
           }
           filled |= 1u << stage;
           if (++stage == kRing) {
@@ -450,25 +458,30 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 // hi = tf32(x) and lo = tf32(x - hi), and
 //   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
 // (the dropped A_lo.B_lo is ~2^-22 relative). The three products are one GEMM
-// over a tripled K: row r of the split operand holds [hi | hi | lo] for A and
-// [hi | lo | hi] for B (B transposed to K-major), each segment Kp = K rounded up
-// to 32 long and zero-padded, so the tensor-core kernel runs unchanged with
-// K' = 3 Kp.
+// over a tripled K' = 3 Kp (Kp = K rounded up to 32, zero-padded): each split
+// operand row holds [hi | lo] (B transposed to K-major), and the TMA producer
+// reads K' segment 0/1/2 from A's hi/hi/lo and B's hi/lo/hi halves.
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
 
-// src[r, k] at src + r*sr + k*sk (R rows, K columns) -> dst[r, seg*Kp + k];
-// lo_seg (1 or 2) is the segment that receives lo. 32x32 tiles through shared
-// memory so both a row-major A and a [K, N] B read and write coalesced.
+// A[r, k] (M rows) and B^T[n, k] (N rows) -> [hi | lo] rows of 2*Kp floats
+// (Kp = K rounded up to 32, zero padded), both operands in one launch
+// (blockIdx.y below mblocks: A, else B). 32x32 tiles through shared memory so
+// both a row-major A and a [K, N] B read and write coalesced.
 __global__ void __launch_bounds__(256)
-tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long long sr, long long sk,
-                  float* __restrict__ dst, long long Kp, int lo_seg) {
+tf32_split_kernel(const float* __restrict__ A, long long M, long long sar, long long sak,
+                  const float* __restrict__ B, long long N, long long sbr, long long sbk, long long K,
+                  float* __restrict__ dA, float* __restrict__ dB, long long Kp, int mblocks) {
   __shared__ float tile[32][33];
+  const bool isA = (int)blockIdx.y < mblocks;
+  const float* src = isA ? A : B;
+  const long long R = isA ? M : N, sr = isA ? sar : sbr, sk = isA ? sak : sbk;
+  float* dst = isA ? dA : dB;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const long long r0 = (long long)blockIdx.y * 32, k0 = (long long)blockIdx.x * 32;
+  const long long r0 = (long long)(isA ? blockIdx.y : blockIdx.y - mblocks) * 32, k0 = (long long)blockIdx.x * 32;
   if (sk == 1) {
 #pragma unroll
     for (int i = ty; i < 32; i += 8) {
@@ -489,11 +502,9 @@ tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long 
     if (r >= R) continue;
     const float x = tile[i][tx];
     const float hi = tf32_rna(x);
-    const float lo = tf32_rna(x - hi);
-    float* d = dst + r * 3 * Kp + k0 + tx;
+    float* d = dst + r * 2 * Kp + k0 + tx;
     d[0] = hi;
-    d[Kp] = lo_seg == 1 ? lo : hi;
-    d[2 * Kp] = lo_seg == 2 ? lo : hi;
+    d[Kp] = tf32_rna(x - hi);
   }
 }
 
@@ -502,6 +513,7 @@ tf32_split_kernel(const float* __restrict__ src, long long R, long long K, long 
 struct LaunchOpts {
   int bn = 256;
   int splits = 1, kb_per_split = 0, m_pad = 0;
+  int tf32_kp_blocks = 1;  // 3xTF32: 32-element K blocks per hi / lo segment
   unsigned long long wait_ns = kWaitLimitNs;
   int stall_producer = 0;
 };
@@ -523,7 +535,7 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   const int kbs = o.splits > 1 ? o.kb_per_split : (int)((K + 31) / 32);  // >= every K-block count
   kern<<<grid, kThreads, smem, st>>>(ta, tb, tc, use_tma, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
                                       alpha, act, idesc, vec_ok, o.wait_ns, o.stall_producer, o.splits,
-                                      kbs, o.m_pad);
+                                      kbs, o.m_pad, o.tf32_kp_blocks);
   B2_CHECK_LAUNCH();
   return B2_OK;
 }
@@ -836,7 +848,7 @@ Tf32Plan tf32_plan(long long M, long long N, long long K, int act) {
 
 size_t tf32_operand_bytes(long long M, long long N, long long K) {
   const long long Kp = (K + 31) / 32 * 32;
-  return ((size_t)(M + N) * 3 * (size_t)Kp * sizeof(float) + 255) / 256 * 256;
+  return ((size_t)(M + N) * 2 * (size_t)Kp * sizeof(float) + 255) / 256 * 256;
 }
 
 size_t gemm_tf32x3_workspace(long long M, long long N, long long K) {
@@ -857,28 +869,25 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
   }
   const long long Kp = (K + 31) / 32 * 32, K3 = 3 * Kp;
   float* Ap = reinterpret_cast<float*>(workspace);
-  float* Bp = Ap + (size_t)M * K3;
+  float* Bp = Ap + (size_t)M * 2 * Kp;
   {
-    const dim3 blk(256);
-    tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)((M + 31) / 32)), blk, 0, st>>>(
-        A, M, K, s[0], s[1], Ap, Kp, 2);
-    B2_CHECK_LAUNCH();
     // B[k, n] at B + k*s[2] + n*s[3]: rows of the split operand are n
-    tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)((N + 31) / 32)), blk, 0, st>>>(
-        B, N, K, s[3], s[2], Bp, Kp, 1);
+    const int mblocks = (int)((M + 31) / 32);
+    tf32_split_kernel<<<dim3((unsigned)(Kp / 32), (unsigned)(mblocks + (N + 31) / 32)), 256, 0, st>>>(
+        A, M, s[0], s[1], B, N, s[3], s[2], K, Ap, Bp, Kp, mblocks);
     B2_CHECK_LAUNCH();
   }
   CUtensorMap ta, tb;
   {
-    const uint64_t dims[2] = {(uint64_t)K3, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)K3 * 4};
+    const uint64_t dims[2] = {(uint64_t)(2 * Kp), (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)(2 * Kp) * 4};
     const uint32_t box[2] = {32, kBM};
     if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Ap, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return B2_ELAUNCH;
   }
   {
-    const uint64_t dims[2] = {(uint64_t)K3, (uint64_t)N};
-    const uint64_t strides[1] = {(uint64_t)K3 * 4};
+    const uint64_t dims[2] = {(uint64_t)(2 * Kp), (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)(2 * Kp) * 4};
     const uint32_t box[2] = {32, 256};
     if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Bp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return B2_ELAUNCH;
@@ -900,6 +909,7 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
     o.splits = plan.splits;
     o.kb_per_split = plan.kb_per_split;
     o.m_pad = (int)plan.m_pad;
+    o.tf32_kp_blocks = (int)(Kp / 32);
     const int rc = launch<float, false, true>(ta, tb, tw, 1, nullptr, B2_F32, W, M, N, K3, plan.np, 1.f,
                                               B2_ACT_NONE, idesc, 1, st, o);
     if (rc != B2_OK) return rc;
@@ -909,6 +919,8 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
       default: return splitk_reduce<float>(W, plan.splits, plan.m_pad, plan.np, bias, bias_dt, C, s[4], M, N, alpha, act, st);
     }
   }
+  LaunchOpts ot;
+  ot.tf32_kp_blocks = (int)(Kp / 32);
   CUtensorMap tc;
   int use_tma = 0;
   if (vec_ok && s[4] >= N) {
@@ -925,11 +937,11 @@ int gemm_tf32x3_launch(const float* A, const float* B, const void* bias, void* C
   if (!use_tma) memset(&tc, 0, sizeof(tc));
   switch (out_dt) {
     case B2_F16:
-      return launch<__half, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
+      return launch<__half, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st, ot);
     case B2_BF16:
-      return launch<__nv_bfloat16, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
+      return launch<__nv_bfloat16, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st, ot);
     case B2_F32:
-      return launch<float, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st);
+      return launch<float, false, true>(ta, tb, tc, use_tma, bias, bias_dt, C, M, N, K3, s[4], alpha, act, idesc, vec_ok, st, ot);
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;
