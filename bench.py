@@ -644,6 +644,8 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
     sus = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
     steps = max(3, min(args.steps, 10))
 
+    pending = []  # (extra key, build whole problem, launch fn) for the T(1) timings
+
     def finish(name, metric_unit, total, shard_work, ms, per, full_ms, kname, err, tol, extra):
         eff = full_ms / (world * ms) if full_ms else None
         if metric_unit == "TFLOP/s":
@@ -701,8 +703,9 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
     ref = O.ref_attention(q[:, i:i + 1].cpu(), k[:, i:i + 1].cpu(), v[:, i:i + 1].cpu(), True)
     err = max(all_gather_floats(O.normwise_err(o[:, i:i + 1], ref), world))
     del q, k, v, o
-    full = full_time(lambda: fa_build(cfg.B * cfg.H, 999),
-                     lambda t: (lambda: b2.flash_attn_fwd(t[0], t[1], t[2], causal=True)))
+    pending.append(("scale_fa", lambda: fa_build(cfg.B * cfg.H, 999),
+                    lambda t: (lambda: b2.flash_attn_fwd(t[0], t[1], t[2], causal=True))))
+    full = None
     e = finish(cfg.name, "TFLOP/s", cfg.flops(), cfg.flops() * n / (cfg.B * cfg.H), ms, per, full,
                kname, err, O.TOL_LOWP_REL + 2.0 ** -8, {"units_rank0": n})
     if do_cpu:
@@ -732,7 +735,8 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
     err = max(all_gather_floats(O.normwise_err(c[r0:r0 + 32], ref), world))
     del a, bm, c
     torch.cuda.empty_cache()
-    full = full_time(lambda: gemm_build(gc.M, 1999), lambda t: (lambda: b2.gemm(t[0], t[1])))
+    pending.append(("scale_gemm", lambda: gemm_build(gc.M, 1999), lambda t: (lambda: b2.gemm(t[0], t[1]))))
+    full = None
     e = finish(gc.name, "TFLOP/s", gc.flops(), 2.0 * (hi - lo) * gc.N * gc.K, ms, per, full, kname,
                err, O.TOL_LOWP_REL + 2.0 ** -8, {"rows_rank0": hi - lo})
     if do_cpu:
@@ -763,13 +767,22 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
             tol = 0.0
         err = max(all_gather_floats(err, world))
         del x, y
-        full = full_time(lambda: rows_build(rc.rows, 2999), lambda t: (lambda: f(t[0])))
+        pending.append((f"scale_rows_{op}", (lambda rb=rows_build: rb(rc.rows, 2999)),
+                        (lambda t, f=f: (lambda: f(t[0])))))
+        full = None
         sub = dataclasses.replace(rc, rows=hi - lo)
         e = finish(f"{rc.name}_{op}", "GB/s", rc.bytes(op), sub.bytes(op), ms, per, full, kname,
                    err, tol, {"rows_rank0": hi - lo})
         if do_cpu:
             e["cpu_baseline"] = cpu_rows(rc, op, args.cpu_seconds_extra, threads, model)
         out[f"scale_rows_{op}"] = e
+    # T(1): rank 0 alone on each whole problem, after every sharded measurement
+    # (so the long single-GPU runs do not heat rank 0 ahead of its shard timings)
+    for key, build, fn_of in pending:
+        full = full_time(build, fn_of)
+        e = out[key]
+        e["full_problem_ms_1gpu"] = round(full, 4) if full else None
+        e["efficiency"] = round(full / (world * e["ms"]), 4) if full else None
     return out
 
 
