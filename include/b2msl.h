@@ -55,6 +55,45 @@ extern "C" {
 #define B2_ACT_SOFTMAX 5   /* softmax over each output row (fused matmul -> row softmax,
                               reference _lowerer_templates.py:1515-1728); needs N <= 256 */
 
+/* Epilogue op codes (b2_gemm_epilogue): each op maps the running fp32 value
+ * x of an output element; a and b are the op's two constants, bias[n] the
+ * column bias. Reference op tables: triton_msl/codegen/_lowerer_templates.py:1733-1748. */
+#define B2_EPI_ADD 1        /* x + a */
+#define B2_EPI_SUB 2        /* x - a */
+#define B2_EPI_RSUB 3       /* a - x */
+#define B2_EPI_MUL 4        /* x * a */
+#define B2_EPI_DIV 5        /* x / a */
+#define B2_EPI_RDIV 6       /* a / x */
+#define B2_EPI_ADD_BIAS 7   /* x + bias[n] */
+#define B2_EPI_MUL_BIAS 8   /* x * bias[n] */
+#define B2_EPI_MAX 9        /* max(x, a), NaN-propagating (tl.maximum) */
+#define B2_EPI_MIN 10       /* min(x, a), NaN-propagating (tl.minimum) */
+#define B2_EPI_MAXNUM 11    /* max(x, a), NaN-quiet (IEEE maxNum) */
+#define B2_EPI_MINNUM 12    /* min(x, a), NaN-quiet */
+#define B2_EPI_CLAMP 13     /* min(max(x, a), b), NaN-propagating (torch.clamp) */
+#define B2_EPI_CLAMPNUM 14  /* min(max(x, a), b), NaN-quiet */
+#define B2_EPI_NEG 15
+#define B2_EPI_EXP 16
+#define B2_EPI_EXP2 17
+#define B2_EPI_LOG 18
+#define B2_EPI_LOG2 19
+#define B2_EPI_SQRT 20
+#define B2_EPI_RSQRT 21
+#define B2_EPI_SIN 22
+#define B2_EPI_COS 23
+#define B2_EPI_ERF 24
+#define B2_EPI_TANH 25
+#define B2_EPI_FLOOR 26
+#define B2_EPI_CEIL 27
+#define B2_EPI_ABS 28
+#define B2_EPI_RELU 29      /* NaN-propagating, like torch.relu */
+#define B2_EPI_GELU 30      /* exact erf GELU */
+#define B2_EPI_GELU_TANH 31
+#define B2_EPI_SILU 32
+#define B2_EPI_SIGMOID 33
+#define B2_EPI_FMA 34       /* x * a + b */
+#define B2_EPI_MAX_OPS 16
+
 /* row operations (b2_row_op) */
 #define B2_ROW_SOFTMAX 0
 #define B2_ROW_LAYERNORM 1
@@ -126,6 +165,23 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C,
             int64_t M, int64_t N, int64_t K, const int64_t strides[6],
             float alpha, int act, int in_dtype, int bias_dtype, int out_dtype,
             void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * GEMM with a general fused epilogue: C = f_n(...f_1(A @ B)) with fp32 math,
+ * f_i given by codes[i] (B2_EPI_*) and the constants args[2i], args[2i+1];
+ * 0 <= n_ops <= B2_EPI_MAX_OPS. The accumulator enters the chain unscaled and
+ * without bias (use B2_EPI_MUL / B2_EPI_ADD_BIAS). Replaces the reference's
+ * fused epilogue lowering of an ordered op chain on the dot result
+ * (_emit_matmul_epilogue_loop, triton_msl/codegen/_lowerer_templates.py:1749-1855,
+ * op tables :1733-1748), which the reference applies only to single-strip
+ * (N <~ 200) matmuls; here any shape, on the same kernels and path selection
+ * as b2_gemm (tensor cores, split-K, CUDA cores). Other arguments as b2_gemm.
+ */
+int b2_gemm_epilogue(const void* A, const void* Bm, const void* bias, void* C,
+                     int64_t M, int64_t N, int64_t K, const int64_t strides[6],
+                     const int32_t* codes, const float* args, int n_ops,
+                     int in_dtype, int bias_dtype, int out_dtype,
+                     void* workspace, size_t ws_bytes, void* stream);
 
 /*
  * Row operation over x[rows, cols] (row stride ld_x elements, unit column stride).

@@ -71,6 +71,57 @@ def ref_gemm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor] = No
     return c.to(out_dtype or a.dtype)
 
 
+def ref_gemm_epilogue(a: torch.Tensor, b: torch.Tensor, ops, bias: Optional[torch.Tensor] = None,
+                      out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """A.float() @ B.float() (tests/test_fast_matmul_parity.py:53), then the op
+    chain in order in fp32, then the cast. Op meanings follow the reference's
+    fused-epilogue tables (triton_msl/codegen/_lowerer_templates.py:1733-1748):
+    max/min propagate NaN (arith.maximumf / minimumf), maxnum/minnum are
+    NaN-quiet (arith.maxnumf / minnumf); clamp propagates NaN like torch.clamp.
+    """
+    x = a.float() @ b.float()
+    bf = bias.float()[None, :] if bias is not None else None
+    for op in ops:
+        n, c = op[0], [float(v) for v in op[1:]]
+        if n == "add": x = x + c[0]
+        elif n == "sub": x = x - c[0]
+        elif n == "rsub": x = c[0] - x
+        elif n == "mul": x = x * c[0]
+        elif n == "div": x = x / c[0]
+        elif n == "rdiv": x = c[0] / x
+        elif n == "add_bias": x = x + bf
+        elif n == "mul_bias": x = x * bf
+        elif n == "max": x = torch.maximum(x, torch.tensor(c[0]))
+        elif n == "min": x = torch.minimum(x, torch.tensor(c[0]))
+        elif n == "maxnum": x = torch.fmax(x, torch.tensor(c[0]))
+        elif n == "minnum": x = torch.fmin(x, torch.tensor(c[0]))
+        elif n == "clamp": x = torch.clamp(x, c[0], c[1])
+        elif n == "clampnum": x = torch.fmin(torch.fmax(x, torch.tensor(c[0])), torch.tensor(c[1]))
+        elif n == "neg": x = -x
+        elif n == "exp": x = torch.exp(x)
+        elif n == "exp2": x = torch.exp2(x)
+        elif n == "log": x = torch.log(x)
+        elif n == "log2": x = torch.log2(x)
+        elif n == "sqrt": x = torch.sqrt(x)
+        elif n == "rsqrt": x = torch.rsqrt(x)
+        elif n == "sin": x = torch.sin(x)
+        elif n == "cos": x = torch.cos(x)
+        elif n == "erf": x = torch.erf(x)
+        elif n == "tanh": x = torch.tanh(x)
+        elif n == "floor": x = torch.floor(x)
+        elif n == "ceil": x = torch.ceil(x)
+        elif n == "abs": x = torch.abs(x)
+        elif n == "relu": x = torch.relu(x)
+        elif n == "gelu": x = torch.nn.functional.gelu(x)
+        elif n == "gelu_tanh": x = torch.nn.functional.gelu(x, approximate="tanh")
+        elif n == "silu": x = torch.nn.functional.silu(x)
+        elif n == "sigmoid": x = torch.sigmoid(x)
+        elif n == "fma": x = x * c[0] + c[1]
+        else:
+            raise ValueError(n)
+    return x.to(out_dtype or a.dtype)
+
+
 def ref_softmax(x: torch.Tensor) -> torch.Tensor:
     """torch.softmax(x, dim=-1) in fp32 (tests/test_integration.py:552)."""
     return torch.softmax(x.float(), dim=-1)

@@ -166,3 +166,40 @@ def test_rewrites_matmul_softmax_into_gemm_epilogue():
     assert "matmul+softmax" in tags
     tags = _rewrite_all(MatmulSoftmax(), torch.randn(64, 32), torch.randn(32, 512))
     assert "matmul+softmax" not in tags    # N > 256: separate softmax
+
+
+class LinearChain(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.fc = nn.Linear(64, 96)
+
+    def forward(self, x, a, b):
+        y = torch.clamp(self.fc(x) * 0.5 - 0.1, min=-1.0, max=2.0).exp()
+        z = torch.sigmoid(1.0 - (a @ b) / 3.0)
+        return y, z, torch.relu(a @ b)
+
+
+def test_rewrites_general_epilogue_chains():
+    tags = _rewrite_all(LinearChain(), torch.randn(8, 64), torch.randn(16, 32), torch.randn(32, 24))
+    # bias, mul, sub, clamp, exp  /  div, rsub, sigmoid  /  a single ReLU stays an activation
+    assert sorted(tags) == sorted(["linear+chain5", "matmul+chain3", "matmul+relu"])
+
+
+@pytest.mark.gpu
+def test_compiled_epilogue_chains_match_fp64_on_gpu():
+    torch.manual_seed(0)
+    m = LinearChain().cuda().half().eval()
+    x = torch.randn(256, 64, device="cuda", dtype=torch.float16)
+    a = torch.randn(256, 128, device="cuda", dtype=torch.float16) / 8
+    b = torch.randn(128, 192, device="cuda", dtype=torch.float16) / 8
+    ref_m = LinearChain().double()
+    ref_m.load_state_dict({k: v.double().cpu() for k, v in m.state_dict().items()})
+    with torch.no_grad():
+        refs = ref_m(x.double().cpu(), a.double().cpu(), b.double().cpu())
+        torch._dynamo.reset()
+        cb.rewrite_log.clear()
+        got = torch.compile(m, backend="b2msl")(x, a, b)
+    assert sorted(cb.rewrite_log) == sorted(["linear+chain5", "matmul+chain3", "matmul+relu"])
+    for g, r in zip(got, refs):
+        err = (g.double().cpu() - r).abs().max().item() / max(r.abs().max().item(), 1e-6)
+        assert err <= 2e-3, err

@@ -21,6 +21,16 @@ B2_OK, B2_EINVAL, B2_EUNSUPPORTED, B2_ELAUNCH, B2_ETIMEOUT = 0, -1, -2, -3, -4
 B2_F32, B2_F16, B2_BF16, B2_I64 = 0, 1, 2, 3
 STATUS_TIMEOUT_TMA, STATUS_TIMEOUT_MMA, STATUS_TIMEOUT_EPI, STATUS_TIMEOUT_SLOT = 1, 2, 4, 8
 ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4, "softmax": 5}
+# b2_gemm_epilogue op codes (B2_EPI_* in include/b2msl.h) and their constant counts
+EPI = {"add": (1, 1), "sub": (2, 1), "rsub": (3, 1), "mul": (4, 1), "div": (5, 1),
+       "rdiv": (6, 1), "add_bias": (7, 0), "mul_bias": (8, 0), "max": (9, 1), "min": (10, 1),
+       "maxnum": (11, 1), "minnum": (12, 1), "clamp": (13, 2), "clampnum": (14, 2),
+       "neg": (15, 0), "exp": (16, 0), "exp2": (17, 0), "log": (18, 0), "log2": (19, 0),
+       "sqrt": (20, 0), "rsqrt": (21, 0), "sin": (22, 0), "cos": (23, 0), "erf": (24, 0),
+       "tanh": (25, 0), "floor": (26, 0), "ceil": (27, 0), "abs": (28, 0), "relu": (29, 0),
+       "gelu": (30, 0), "gelu_tanh": (31, 0), "silu": (32, 0), "sigmoid": (33, 0),
+       "fma": (34, 2)}
+EPI_MAX_OPS = 16
 ROW_OPS = {"softmax": 0, "layernorm": 1, "rmsnorm": 2, "sum": 3, "max": 4,
            "argmax": 5, "min": 6, "argmin": 7}
 
@@ -35,6 +45,10 @@ SIGNATURES = {
     "b2_gemm": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
                 + [_c_i64p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                    ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b2_gemm_epilogue": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+                         + [_c_i64p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_float),
+                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "b2_row_op": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4
                   + [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                      ctypes.c_void_p]),

@@ -39,6 +39,7 @@ import torch.nn.functional as F
 from . import ops as b2ops
 
 _FLOATS = (torch.float32, torch.float16, torch.bfloat16)
+_EPI_MAX = 16
 
 
 def _val(n):
@@ -117,6 +118,88 @@ def _matmul_act(a, b, act):
 
 def _addmm_act(bias, a, b, act):
     return b2ops.gemm(a, b, bias, act)
+
+
+def _linear_chain(x, w, b, codes, args):
+    """x[..., K] @ w[N, K]^T with a general epilogue chain (bias first when given)."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    y = torch.ops.b2msl.gemm_epilogue(x2, w.t(), b, list(codes), list(args), None)
+    return y.reshape(*lead, w.shape[0])
+
+
+def _matmul_chain(a, b, bias, codes, args):
+    return torch.ops.b2msl.gemm_epilogue(a, b, bias, list(codes), list(args), None)
+
+
+def _num(x) -> bool:
+    return isinstance(x, (int, float)) and not isinstance(x, bool)
+
+
+_UNARY_EPI = {torch.exp: "exp", torch.exp2: "exp2", torch.log: "log", torch.log2: "log2",
+              torch.sqrt: "sqrt", torch.rsqrt: "rsqrt", torch.sin: "sin", torch.cos: "cos",
+              torch.erf: "erf", torch.special.erf: "erf", torch.tanh: "tanh", torch.floor: "floor",
+              torch.ceil: "ceil", torch.abs: "abs", torch.sigmoid: "sigmoid", F.sigmoid: "sigmoid",
+              torch.neg: "neg", operator.neg: "neg", torch.relu: "relu", F.relu: "relu",
+              F.silu: "silu", "exp": "exp", "exp2": "exp2", "log": "log", "log2": "log2",
+              "sqrt": "sqrt", "rsqrt": "rsqrt", "sin": "sin", "cos": "cos", "erf": "erf",
+              "tanh": "tanh", "floor": "floor", "ceil": "ceil", "abs": "abs",
+              "sigmoid": "sigmoid", "neg": "neg", "relu": "relu"}
+
+
+def _epi_step(u: fx.Node, prev: fx.Node):
+    """The epilogue op(s) element-wise node u applies to its input prev, or None.
+    Constants must be Python numbers (the traced graph's literals)."""
+    if u.op not in ("call_function", "call_method"):
+        return None
+    t = _target_key(u)
+    kw = {k: v for k, v in u.kwargs.items() if not (k == "inplace" and v is False)}
+    a = u.args
+    try:
+        if t in _UNARY_EPI and len(a) == 1 and a[0] is prev and not kw:
+            return [(_UNARY_EPI[t],)]
+    except TypeError:
+        return None
+    if t is F.gelu and len(a) == 1 and a[0] is prev and kw.get("approximate", "none") in ("none", "tanh") \
+            and set(kw) <= {"approximate"}:
+        return [("gelu_tanh",) if kw.get("approximate") == "tanh" else ("gelu",)]
+    if kw:
+        if t in (torch.clamp, "clamp", torch.clip, "clip") and len(a) == 1 and a[0] is prev \
+                and set(kw) <= {"min", "max"}:
+            lo, hi = kw.get("min"), kw.get("max")
+            if (lo is None or _num(lo)) and (hi is None or _num(hi)):
+                return [("clamp", float("-inf") if lo is None else lo, float("inf") if hi is None else hi)]
+        return None
+    if t in (torch.clamp, "clamp", torch.clip, "clip") and 2 <= len(a) <= 3 and a[0] is prev:
+        lo = a[1]
+        hi = a[2] if len(a) == 3 else None
+        if (lo is None or _num(lo)) and (hi is None or _num(hi)):
+            return [("clamp", float("-inf") if lo is None else lo, float("inf") if hi is None else hi)]
+        return None
+    if len(a) != 2:
+        return None
+    x, y = a
+    if t in (operator.add, torch.add, "add", operator.iadd):
+        if x is prev and _num(y):
+            return [("add", y)]
+        if y is prev and _num(x):
+            return [("add", x)]
+    if t in (operator.sub, torch.sub, "sub", operator.isub):
+        if x is prev and _num(y):
+            return [("sub", y)]
+        if y is prev and _num(x):
+            return [("rsub", x)]
+    if t in (operator.mul, torch.mul, "mul", operator.imul):
+        if x is prev and _num(y):
+            return [("mul", y)]
+        if y is prev and _num(x):
+            return [("mul", x)]
+    if t in (operator.truediv, torch.div, "div", torch.true_divide, "true_divide"):
+        if x is prev and _num(y):
+            return [("div", y)]
+        if y is prev and _num(x):
+            return [("rdiv", x)]
+    return None
 
 
 def _sdpa(q, k, v, causal, scale):
@@ -207,6 +290,25 @@ class Rewriter:
         self.replaced.append(tag)
         return new
 
+    def _epilogue_chain(self, node: fx.Node, has_bias: bool):
+        """The longest run of single-user element-wise nodes after `node` that the
+        general GEMM epilogue expresses (reference op chain, _lowerer_templates.py:
+        1733-1855). Returns (last node, ops) when it is more than one activation."""
+        ops = [("add_bias",)] if has_bias else []
+        prev, last = node, None
+        while len(prev.users) == 1 and len(ops) < _EPI_MAX:
+            u = next(iter(prev.users))
+            step = _epi_step(u, prev)
+            v = _val(u)
+            if step is None or not isinstance(v, torch.Tensor) or v.dtype != _val(node).dtype:
+                break
+            ops += step
+            prev = last = u
+        body = ops[1:] if has_bias else ops
+        if last is None or (len(body) == 1 and body[0][0] in ("relu", "gelu", "gelu_tanh", "silu")):
+            return None, None
+        return last, ops
+
     def _single_user_act(self, node: fx.Node):
         users = list(node.users)
         if len(users) != 1:
@@ -294,6 +396,12 @@ class Rewriter:
                     return
             a, b = node.args
             if _ok_tensor(a, ac, 2) and _ok_tensor(b, ac, 2) and _val(a).dtype == _val(b).dtype:
+                last, ops = self._epilogue_chain(node, False)
+                if last is not None:
+                    codes, args = b2ops._epi_program(ops)
+                    self._replace(node, _matmul_chain, (a, b, None, codes, args),
+                                  f"matmul+chain{len(ops)}", last)
+                    return
                 act_node, act = self._single_user_act(node)
                 self._replace(node, _matmul_act, (a, b, act or "none"),
                               "matmul" + (f"+{act}" if act else ""), act_node)
@@ -304,6 +412,12 @@ class Rewriter:
             b = _arg(node, 2, "bias")
             if _ok_tensor(x, ac) and _ok_tensor(w, ac, 2) and _val(x).dtype == _val(w).dtype \
                     and (b is None or _ok_tensor(b, ac, 1)):
+                last, ops = self._epilogue_chain(node, b is not None)
+                if last is not None:
+                    codes, args = b2ops._epi_program(ops)
+                    self._replace(node, _linear_chain, (x, w, b, codes, args),
+                                  f"linear+chain{len(ops)}", last)
+                    return
                 act_node, act = self._single_user_act(node)
                 self._replace(node, _linear_act, (x, w, b, act or "none"),
                               "linear" + (f"+{act}" if act else ""), act_node)
@@ -311,6 +425,12 @@ class Rewriter:
         if t is torch.addmm and len(node.args) == 3 and not node.kwargs:
             bias, a, b = node.args
             if _ok_tensor(bias, ac, 1) and _ok_tensor(a, ac, 2) and _ok_tensor(b, ac, 2):
+                last, ops = self._epilogue_chain(node, True)
+                if last is not None:
+                    codes, args = b2ops._epi_program(ops)
+                    self._replace(node, _matmul_chain, (a, b, bias, codes, args),
+                                  f"addmm+chain{len(ops)}", last)
+                    return
                 act_node, act = self._single_user_act(node)
                 self._replace(node, _addmm_act, (bias, a, b, act or "none"),
                               "addmm" + (f"+{act}" if act else ""), act_node)

@@ -81,6 +81,68 @@ __device__ __forceinline__ float apply_act(float x, int act) {
   }
 }
 
+// ---- general epilogue chains (b2_gemm_epilogue)
+// Internal activation code that selects the chain in every GEMM kernel.
+constexpr int kActChain = 6;
+constexpr int kMaxEpiOps = B2_EPI_MAX_OPS;
+// Passed by value as a kernel parameter.
+struct EpiProgram {
+  int n;
+  int code[kMaxEpiOps];
+  float a[kMaxEpiOps];
+  float b[kMaxEpiOps];
+};
+// The chain of the b2_gemm_epilogue call running on this host thread (n = 0
+// otherwise); every GEMM launch copies it into its kernel's parameters.
+const EpiProgram& epi_program();
+void set_epi_program(const EpiProgram* p);
+
+__device__ __forceinline__ float epi_op(float x, int code, float a, float b, float bias) {
+  switch (code) {
+    case B2_EPI_ADD: return x + a;
+    case B2_EPI_SUB: return x - a;
+    case B2_EPI_RSUB: return a - x;
+    case B2_EPI_MUL: return x * a;
+    case B2_EPI_DIV: return x / a;
+    case B2_EPI_RDIV: return a / x;
+    case B2_EPI_ADD_BIAS: return x + bias;
+    case B2_EPI_MUL_BIAS: return x * bias;
+    case B2_EPI_MAX: return (x != x || a != a) ? __int_as_float(0x7fffffff) : fmaxf(x, a);
+    case B2_EPI_MIN: return (x != x || a != a) ? __int_as_float(0x7fffffff) : fminf(x, a);
+    case B2_EPI_MAXNUM: return fmaxf(x, a);
+    case B2_EPI_MINNUM: return fminf(x, a);
+    case B2_EPI_CLAMP: return x != x ? x : fminf(fmaxf(x, a), b);
+    case B2_EPI_CLAMPNUM: return fminf(fmaxf(x, a), b);
+    case B2_EPI_NEG: return -x;
+    case B2_EPI_EXP: return expf(x);
+    case B2_EPI_EXP2: return exp2f(x);
+    case B2_EPI_LOG: return logf(x);
+    case B2_EPI_LOG2: return log2f(x);
+    case B2_EPI_SQRT: return sqrtf(x);
+    case B2_EPI_RSQRT: return rsqrtf(x);
+    case B2_EPI_SIN: return sinf(x);
+    case B2_EPI_COS: return cosf(x);
+    case B2_EPI_ERF: return erff(x);
+    case B2_EPI_TANH: return tanhf(x);
+    case B2_EPI_FLOOR: return floorf(x);
+    case B2_EPI_CEIL: return ceilf(x);
+    case B2_EPI_ABS: return fabsf(x);
+    case B2_EPI_RELU: return apply_act(x, B2_ACT_RELU);
+    case B2_EPI_GELU: return apply_act(x, B2_ACT_GELU);
+    case B2_EPI_GELU_TANH: return apply_act(x, B2_ACT_GELU_TANH);
+    case B2_EPI_SILU: return x / (1.f + expf(-x));
+    case B2_EPI_SIGMOID: return 1.f / (1.f + expf(-x));
+    case B2_EPI_FMA: return fmaf(x, a, b);
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ float epi_chain(float x, float bias, const EpiProgram& p) {
+#pragma unroll 1
+  for (int o = 0; o < p.n; ++o) x = epi_op(x, p.code[o], p.a[o], p.b[o], bias);
+  return x;
+}
+
 }  // namespace b2
 
 #define B2_CUDA_TRY(expr)                                                        \

@@ -73,6 +73,15 @@ void set_error(const char* fmt, ...) {
 }
 void clear_error() { t_err.clear(); }
 
+namespace {
+thread_local EpiProgram t_epi = {};
+}
+const EpiProgram& epi_program() { return t_epi; }
+void set_epi_program(const EpiProgram* p) {
+  if (p) t_epi = *p;
+  else t_epi.n = 0;
+}
+
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
@@ -140,10 +149,10 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, i
   return rc;
 }
 
-int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
-            int64_t K, const int64_t strides[6], float alpha, int act, int in_dtype,
-            int bias_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
-  clear_error();
+namespace {
+int gemm_impl(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
+              int64_t K, const int64_t strides[6], float alpha, int act, int in_dtype,
+              int bias_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
   if (M < 0 || N < 0 || K < 0) {
     set_error("b2_gemm: invalid shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
     return B2_EINVAL;
@@ -154,7 +163,7 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
               out_dtype);
     return B2_EINVAL;
   }
-  if (act < B2_ACT_NONE || act > B2_ACT_SOFTMAX) {
+  if (act < B2_ACT_NONE || (act > B2_ACT_SOFTMAX && act != kActChain)) {
     set_error("b2_gemm: unknown activation %d", act);
     return B2_EINVAL;
   }
@@ -211,6 +220,52 @@ int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M,
                           out_dtype, st);
     if (rc == B2_OK) t_kernel = "gemm_simt";
   }
+  return rc;
+}
+
+}  // namespace
+
+int b2_gemm(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
+            int64_t K, const int64_t strides[6], float alpha, int act, int in_dtype,
+            int bias_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  if (act == kActChain) {
+    set_error("b2_gemm: unknown activation %d", act);
+    return B2_EINVAL;
+  }
+  set_epi_program(nullptr);
+  return gemm_impl(A, Bm, bias, C, M, N, K, strides, alpha, act, in_dtype, bias_dtype, out_dtype,
+                   workspace, ws_bytes, stream);
+}
+
+int b2_gemm_epilogue(const void* A, const void* Bm, const void* bias, void* C, int64_t M, int64_t N,
+                     int64_t K, const int64_t strides[6], const int32_t* codes, const float* args,
+                     int n_ops, int in_dtype, int bias_dtype, int out_dtype, void* workspace,
+                     size_t ws_bytes, void* stream) {
+  clear_error();
+  if (n_ops < 0 || n_ops > kMaxEpiOps || (n_ops > 0 && (!codes || !args))) {
+    set_error("b2_gemm_epilogue: need 0 <= n_ops <= %d with codes and args", kMaxEpiOps);
+    return B2_EINVAL;
+  }
+  EpiProgram prog = {};
+  prog.n = n_ops;
+  for (int i = 0; i < n_ops; ++i) {
+    if (codes[i] < B2_EPI_ADD || codes[i] > B2_EPI_FMA) {
+      set_error("b2_gemm_epilogue: unknown op code %d at position %d", codes[i], i);
+      return B2_EINVAL;
+    }
+    if ((codes[i] == B2_EPI_ADD_BIAS || codes[i] == B2_EPI_MUL_BIAS) && !bias) {
+      set_error("b2_gemm_epilogue: op %d at position %d needs a bias vector", codes[i], i);
+      return B2_EINVAL;
+    }
+    prog.code[i] = codes[i];
+    prog.a[i] = args[2 * i];
+    prog.b[i] = args[2 * i + 1];
+  }
+  set_epi_program(&prog);
+  const int rc = gemm_impl(A, Bm, bias, C, M, N, K, strides, 1.f, kActChain, in_dtype, bias_dtype,
+                           out_dtype, workspace, ws_bytes, stream);
+  set_epi_program(nullptr);
   return rc;
 }
 

@@ -22,7 +22,8 @@ template <typename TI, typename TO, typename TB>
 __global__ void __launch_bounds__(NT)
 gemm_simt_kernel(const TI* __restrict__ A, const TI* __restrict__ B, const TB* __restrict__ bias,
                  TO* __restrict__ C, int M, int N, int K, long long sam, long long sak,
-                 long long sbk, long long sbn, long long scm, long long scn, float alpha, int act) {
+                 long long sbk, long long sbn, long long scm, long long scn, float alpha, int act,
+                 const EpiProgram prog) {
   __shared__ __align__(16) float As[2][BK][BM];
   __shared__ __align__(16) float Bs[2][BK][BN];
   const int tid = threadIdx.x;
@@ -95,6 +96,10 @@ gemm_simt_kernel(const TI* __restrict__ A, const TI* __restrict__ B, const TB* _
       const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
       if (n >= N) continue;
       float c = acc[i][j] * alpha;
+      if (act == kActChain) {
+        C[m * scm + n * scn] = from_f32<TO>(epi_chain(c, bias ? to_f32<TB>(bias[n]) : 0.f, prog));
+        continue;
+      }
       if (bias) c += to_f32<TB>(bias[n]);
       C[m * scm + n * scn] = from_f32<TO>(apply_act(c, act));
     }
@@ -107,7 +112,7 @@ int launch3(const void* A, const void* B, const void* bias, void* C, long long M
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
   gemm_simt_kernel<TI, TO, TB><<<grid, NT, 0, st>>>((const TI*)A, (const TI*)B, (const TB*)bias,
                                                     (TO*)C, (int)M, (int)N, (int)K, s[0], s[1],
-                                                    s[2], s[3], s[4], s[5], alpha, act);
+                                                    s[2], s[3], s[4], s[5], alpha, act, epi_program());
   B2_CHECK_LAUNCH();
   return B2_OK;
 }

@@ -107,7 +107,7 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                   const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, int M, int N,
                   int K, long long ldc, float alpha, int act, uint32_t idesc, int vec_ok,
                   unsigned long long wait_ns, int stall_producer, int splits, int kb_per_split,
-                  int m_pad, int tf32_kp_blocks) {
+                  int m_pad, int tf32_kp_blocks, const EpiProgram prog) {
   using Cfg = EpiCfg<TO, BN>;
   constexpr int kBN = BN;
   constexpr int kRing = Cfg::kRing;
@@ -374,6 +374,10 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           case B2_ACT_GELU: act_chunk<B2_ACT_GELU>(f, r, bv, alpha); break;
           case B2_ACT_GELU_TANH: act_chunk<B2_ACT_GELU_TANH>(f, r, bv, alpha); break;
           case B2_ACT_SILU: act_chunk<B2_ACT_SILU>(f, r, bv, alpha); break;
+          case kActChain:
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) f[j] = epi_chain(__uint_as_float(r[j]) * alpha, bv[j], prog);
+            break;
           default: act_chunk<B2_ACT_NONE>(f, r, bv, alpha); break;
         }
         if (act == B2_ACT_SOFTMAX) {
@@ -535,7 +539,7 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   const int kbs = o.splits > 1 ? o.kb_per_split : (int)((K + 31) / 32);  // >= every K-block count
   kern<<<grid, kThreads, smem, st>>>(ta, tb, tc, use_tma, bias, bias_dt, (TO*)C, (int)M, (int)N, (int)K, ldc,
                                       alpha, act, idesc, vec_ok, o.wait_ns, o.stall_producer, o.splits,
-                                      kbs, o.m_pad, o.tf32_kp_blocks);
+                                      kbs, o.m_pad, o.tf32_kp_blocks, epi_program());
   B2_CHECK_LAUNCH();
   return B2_OK;
 }
@@ -572,7 +576,7 @@ template <typename TO, int ACT>
 __global__ void __launch_bounds__(256)
 gemm_splitk_reduce_kernel(const float* __restrict__ W, int splits, long long m_pad, long long np,
                           const void* __restrict__ bias, int bias_dt, TO* __restrict__ C, long long ldc,
-                          int M, int N, float alpha) {
+                          int M, int N, float alpha, const EpiProgram prog) {
   const long long n4 = (N + 3) / 4;
   const long long total = (long long)M * n4;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -590,7 +594,8 @@ gemm_splitk_reduce_kernel(const float* __restrict__ W, int splits, long long m_p
     for (int e = 0; e < 4; ++e) {
       if (n + e >= N) break;
       const float bv = bias ? bias_at(bias, bias_dt, n + e) : 0.f;
-      crow[n + e] = from_f32<TO>(apply_act(fmaf(a[e], alpha, bv), ACT));
+      crow[n + e] = from_f32<TO>(ACT == kActChain ? epi_chain(a[e] * alpha, bv, prog)
+                                                  : apply_act(fmaf(a[e], alpha, bv), ACT));
     }
   }
 }
@@ -605,14 +610,16 @@ int splitk_reduce(const float* W, int splits, long long m_pad, long long np, con
   TO* c = reinterpret_cast<TO*>(C);
   switch (act) {
 #define B2_SPLITK_CASE(A) \
-  case A: gemm_splitk_reduce_kernel<TO, A><<<(unsigned)blocks, 256, 0, st>>>(W, splits, m_pad, np, bias, bias_dt, c, ldc, (int)M, (int)N, alpha); break;
+  case A: gemm_splitk_reduce_kernel<TO, A><<<(unsigned)blocks, 256, 0, st>>>(W, splits, m_pad, np, bias, bias_dt, c, ldc, (int)M, (int)N, alpha, epi_program()); break;
     B2_SPLITK_CASE(B2_ACT_RELU)
     B2_SPLITK_CASE(B2_ACT_GELU)
     B2_SPLITK_CASE(B2_ACT_GELU_TANH)
     B2_SPLITK_CASE(B2_ACT_SILU)
+    B2_SPLITK_CASE(kActChain)
     default:
       gemm_splitk_reduce_kernel<TO, B2_ACT_NONE><<<(unsigned)blocks, 256, 0, st>>>(W, splits, m_pad, np, bias,
-                                                                                 bias_dt, c, ldc, (int)M, (int)N, alpha);
+                                                                                 bias_dt, c, ldc, (int)M, (int)N, alpha,
+                                                                                 epi_program());
 #undef B2_SPLITK_CASE
   }
   B2_CHECK_LAUNCH();

@@ -85,7 +85,7 @@ template <typename TO, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const void* __restrict__ bias, int bias_dt,
-                 int M, int N, int K, float alpha, int act, uint32_t idesc) {
+                 int M, int N, int K, float alpha, int act, uint32_t idesc, const EpiProgram prog) {
   constexpr int kRing = PairCfg<TO>::kRing;
   constexpr uint32_t kStageOutBytes = PairCfg<TO>::kOutBytes;
   extern __shared__ uint8_t smem_raw[];
@@ -284,6 +284,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           case B2_ACT_GELU: pair_act_chunk<B2_ACT_GELU>(f, r, bv, alpha); break;
           case B2_ACT_GELU_TANH: pair_act_chunk<B2_ACT_GELU_TANH>(f, r, bv, alpha); break;
           case B2_ACT_SILU: pair_act_chunk<B2_ACT_SILU>(f, r, bv, alpha); break;
+          case kActChain:
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) f[j] = epi_chain(__uint_as_float(r[j]) * alpha, bv[j], prog);
+            break;
           default: pair_act_chunk<B2_ACT_NONE>(f, r, bv, alpha); break;
         }
         constexpr int RB = 32 * (int)sizeof(TO);
@@ -342,7 +346,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const long long tiles = ((M + kPM - 1) / kPM) * ((N + kBN - 1) / kBN);
   const long long pairs = tiles < sms / 2 ? tiles : sms / 2;
   kern<<<(unsigned)(2 * pairs), kThreads, smem, st>>>(ta, tb, tc, bias, bias_dt, (int)M, (int)N, (int)K, alpha,
-                                                      act, idesc);
+                                                      act, idesc, epi_program());
   B2_CHECK_LAUNCH();
   return B2_OK;
 }

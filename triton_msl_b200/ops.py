@@ -18,7 +18,8 @@ Inputs must be CUDA tensors; anything else raises (no CPU fallback).
 from __future__ import annotations
 
 import math
-from typing import Optional
+import ctypes
+from typing import List, Optional, Sequence
 
 import torch
 
@@ -152,6 +153,83 @@ def gemm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor] = None,
     each output row, the reference's fused matmul + row-softmax; N <= 256).
     """
     return torch.ops.b2msl.gemm(a, b, bias, activation, out_dtype, float(alpha))
+
+
+def _epi_program(ops):
+    """[(name, *constants)] -> (codes, args) for b2_gemm_epilogue."""
+    codes, args = [], []
+    for op in ops:
+        name, consts = op[0], [float(c) for c in op[1:]]
+        if name not in _lib.EPI:
+            raise ValueError(f"gemm_epilogue: unknown op {name!r} (one of {sorted(_lib.EPI)})")
+        code, n = _lib.EPI[name]
+        if len(consts) != n:
+            raise ValueError(f"gemm_epilogue: op {name!r} takes {n} constant(s), got {len(consts)}")
+        codes.append(code)
+        args += (consts + [0.0, 0.0])[:2]
+    if len(codes) > _lib.EPI_MAX_OPS:
+        raise ValueError(f"gemm_epilogue: at most {_lib.EPI_MAX_OPS} ops")
+    return codes, args
+
+
+def _gemm_epi_impl(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor], codes: List[int],
+                   args: List[float], out_dtype: Optional[torch.dtype]) -> torch.Tensor:
+    what = "gemm_epilogue"
+    dev = _require_cuda(a, b, bias, what=what)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"{what}: need a[M,K] @ b[K,N]; got {tuple(a.shape)} @ {tuple(b.shape)}")
+    if a.dtype != b.dtype:
+        raise TypeError(f"{what}: a and b must share a dtype ({a.dtype} vs {b.dtype})")
+    M, K = a.shape
+    N = b.shape[1]
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != N):
+        raise ValueError(f"{what}: bias must be [N={N}]")
+    c = torch.empty((M, N), dtype=out_dtype or a.dtype, device=dev)
+    strides = [a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)]
+    n = len(codes)
+    codes_c = (ctypes.c_int32 * max(n, 1))(*codes)
+    args_c = (ctypes.c_float * max(2 * n, 2))(*args)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        ws_bytes = L.b2_query_workspace(0, M, N, K, _dtype_code(a, what))
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev) if ws_bytes else None
+        st = L.b2_gemm_epilogue(a.data_ptr(), b.data_ptr(),
+                                bias.data_ptr() if bias is not None else None, c.data_ptr(),
+                                M, N, K, _lib.i64_array(strides), codes_c, args_c, n,
+                                _dtype_code(a, what),
+                                _dtype_code(bias, what) if bias is not None else _lib.B2_F32,
+                                _dtype_code(c, what), ws.data_ptr() if ws is not None else None,
+                                ws_bytes, _stream(dev))
+    _lib.check("b2_gemm_epilogue", st)
+    return c
+
+
+@torch.library.custom_op("b2msl::gemm_epilogue", mutates_args=())
+def _gemm_epi_op(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor], codes: List[int],
+                 args: List[float], out_dtype: Optional[torch.dtype]) -> torch.Tensor:
+    return _gemm_epi_impl(a, b, bias, codes, args, out_dtype)
+
+
+@_gemm_epi_op.register_fake
+def _(a, b, bias, codes, args, out_dtype):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype or a.dtype)
+
+
+def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, ops: Sequence[tuple],
+                  bias: Optional[torch.Tensor] = None,
+                  out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """c = f_n(...f_1(a @ b)) with fp32 math: a general fused epilogue chain.
+
+    ops: sequence of (name, *constants), applied in order to each output
+    element, e.g. [("add_bias",), ("mul", 0.5), ("clamp", -1.0, 1.0), ("exp",)].
+    Names: add sub rsub mul div rdiv (one constant), add_bias mul_bias (bias[n]),
+    max min (NaN-propagating) maxnum minnum (NaN-quiet), clamp clampnum (two),
+    neg exp exp2 log log2 sqrt rsqrt sin cos erf tanh floor ceil abs relu gelu
+    gelu_tanh silu sigmoid, fma (x * c0 + c1). The reference lowers such chains
+    for single-strip matmuls only (_lowerer_templates.py:1749-1855).
+    """
+    codes, args = _epi_program(ops)
+    return torch.ops.b2msl.gemm_epilogue(a, b, bias, codes, args, out_dtype)
 
 
 # ---------------------------------------------------------------- row family
