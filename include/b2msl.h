@@ -237,10 +237,26 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out,
 int b2_row_reduce_noalloc(int op, const void* x, void* out, int64_t rows, int64_t cols,
                           int64_t ld_x, int dtype, void* stream);
 
+/*
+ * Reduction over the middle axis of a contiguous x[outer, R, inner]:
+ * out[o, i] = reduce over r of x[o, r, i] (torch's sum / amax / amin / argmax /
+ * argmin along a dimension that is not the last one: x viewed as
+ * [prod(dims before), size(dim), prod(dims after)]). Replaces the reference's
+ * generic tt.reduce lowering for non-last axes (triton_msl/codegen/_lowerer_reduce.py:773-1010,
+ * fuzzed as 2d_sum_ax0 / 3d_sum_ax0 in tests/test_fuzz_reduce.py:88-139).
+ * op: B2_ROW_SUM / MAX / MIN / ARGMAX / ARGMIN (NaN and tie rules as b2_row_op);
+ * out: x's dtype, or int64 indices in [0, R) for argmax/argmin. workspace: size
+ * from b2_query_workspace(3, outer, R, inner, 0) (splits R across CTAs when the
+ * output is small); without it one pass runs.
+ */
+int b2_reduce_axis(int op, const void* x, void* out, int64_t outer, int64_t R, int64_t inner,
+                   int dtype, void* workspace, size_t ws_bytes, void* stream);
+
 /* Scratch bytes a call with these arguments needs (0 = none).
  * kind: 0 = b2_gemm (a0=M, a1=N, a2=K, a3=in_dtype),
  *       1 = b2_row_op (a0=op, a1=rows, a2=cols, a3=dtype),
- *       2 = b2_fa_fwd (always 0). */
+ *       2 = b2_fa_fwd (always 0),
+ *       3 = b2_reduce_axis (a0=outer, a1=R, a2=inner). */
 size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3);
 
 /* OR of the device status bits written by bounded waits on `device` since the

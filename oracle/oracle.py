@@ -165,6 +165,23 @@ def ref_argmin(x: torch.Tensor) -> torch.Tensor:
     return x.float().argmin(-1)
 
 
+def ref_reduce_axis(x: torch.Tensor, op: str, dim: int) -> torch.Tensor:
+    """A.float().sum(dim) / .max(dim).values / .min(dim).values / .argmax(dim) /
+    .argmin(dim) (tests/test_fuzz_reduce.py:88-139: 2d_sum_ax0, 3d_sum_ax0)."""
+    xf = x.float()
+    if op == "sum":
+        return xf.sum(dim)
+    if op == "max":
+        return xf.max(dim).values
+    if op == "min":
+        return xf.min(dim).values
+    if op == "argmax":
+        return xf.argmax(dim)
+    if op == "argmin":
+        return xf.argmin(dim)
+    raise ValueError(op)
+
+
 ROW_REFS = {
     "softmax": lambda x, w, b, eps: ref_softmax(x),
     "layernorm": lambda x, w, b, eps: ref_layernorm(x, w, b, eps),

@@ -203,3 +203,13 @@ def test_compiled_epilogue_chains_match_fp64_on_gpu():
     for g, r in zip(got, refs):
         err = (g.double().cpu() - r).abs().max().item() / max(r.abs().max().item(), 1e-6)
         assert err <= 2e-3, err
+
+
+class AxisReductions(nn.Module):
+    def forward(self, x, y):
+        return x.sum(0), torch.amax(y, dim=1), y.argmin(dim=0), x.sum(-1)
+
+
+def test_rewrites_reductions_along_any_axis():
+    tags = _rewrite_all(AxisReductions(), torch.randn(64, 96), torch.randn(8, 16, 32))
+    assert sorted(tags) == sorted(["reduce_sum(dim)", "reduce_max(dim)", "reduce_argmin(dim)", "row_sum"])

@@ -8,7 +8,7 @@ ops plus a ``torch.compile`` backend (``backend="b2msl"``).
 from ._lib import B2Error, B2Unsupported, last_kernel, device_status  # noqa: F401
 from .ops import (  # noqa: F401
     flash_attn_fwd, gemm, gemm_epilogue, row_softmax, row_layernorm, row_rmsnorm, row_sum, row_max,
-    row_min, row_argmax, row_argmin,
+    row_min, row_argmax, row_argmin, reduce,
 )
 from .host_pipeline import flash_attn_fwd_host  # noqa: F401
 

@@ -49,6 +49,9 @@ SIGNATURES = {
                          + [_c_i64p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_float),
                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "b2_reduce_axis": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+                       + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                                  ctypes.c_void_p]),
     "b2_row_op": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4
                   + [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                      ctypes.c_void_p]),

@@ -264,6 +264,10 @@ def _rowred(x, kind):
     return getattr(b2ops, f"row_{kind}")(x)
 
 
+def _axisred(x, kind, dim):
+    return b2ops.reduce(x, kind, dim)
+
+
 def _layer_norm(x, w, b, eps):
     return b2ops.row_layernorm(x, w, b, eps)
 
@@ -472,6 +476,11 @@ class Rewriter:
             if _ok_tensor(x, ac) and _is_last_dim(dim, xv) and not keep and node.kwargs.get("dtype") is None \
                     and xv.dim() >= 1 and xv.shape[-1] > 0:
                 self._replace(node, _rowred, (x, kind), f"row_{kind}")
+            elif _ok_tensor(x, ac) and not keep and node.kwargs.get("dtype") is None and xv.dim() >= 2:
+                # one other axis: the middle-axis reduction
+                d = dim[0] if isinstance(dim, (list, tuple)) and len(dim) == 1 else dim
+                if isinstance(d, int) and -xv.dim() <= d < xv.dim() and xv.shape[d] > 0:
+                    self._replace(node, _axisred, (x, kind, int(d)), f"reduce_{kind}(dim)")
             return
 
     def _attn_weights_ok(self, E, H, *ps) -> bool:

@@ -32,6 +32,9 @@ int row_op_launch(int, const void*, const void*, const void*, void*, long long, 
                   long long, long long, float, int, void*, size_t, cudaStream_t);
 int gemm_stall_test_launch(const void*, const void*, void*, long long, long long, long long,
                            unsigned long long, cudaStream_t);
+size_t axis_reduce_workspace(long long, long long, long long);
+int axis_reduce_launch(int, const void*, void*, long long, long long, long long, int, void*, size_t,
+                       cudaStream_t);
 uint32_t row_read_status(bool);
 uint32_t gemm_read_status(bool);
 uint32_t pair_read_status(bool);
@@ -317,6 +320,43 @@ int b2_row_op(int op, const void* x, const void* w, const void* b, void* out, in
   return rc;
 }
 
+int b2_reduce_axis(int op, const void* x, void* out, int64_t outer, int64_t R, int64_t inner,
+                   int dtype, void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  if (op != B2_ROW_SUM && op != B2_ROW_MAX && op != B2_ROW_MIN && op != B2_ROW_ARGMAX &&
+      op != B2_ROW_ARGMIN) {
+    set_error("b2_reduce_axis: op %d is not sum/max/min/argmax/argmin", op);
+    return B2_EINVAL;
+  }
+  if (!valid_float_dtype(dtype)) {
+    set_error("b2_reduce_axis: unsupported dtype %d", dtype);
+    return B2_EINVAL;
+  }
+  if (outer < 0 || R < 0 || inner < 0) {
+    set_error("b2_reduce_axis: invalid shape outer=%lld R=%lld inner=%lld", (long long)outer,
+              (long long)R, (long long)inner);
+    return B2_EINVAL;
+  }
+  if (R == 0 && op != B2_ROW_SUM && outer * inner > 0) {
+    set_error("b2_reduce_axis: max/min/argmax/argmin over an empty axis is undefined");
+    return B2_EINVAL;
+  }
+  if (outer == 0 || inner == 0) return B2_OK;
+  if (!out || (R > 0 && !x)) {
+    set_error("b2_reduce_axis: null pointer argument");
+    return B2_EINVAL;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (R == 0) {  // sum over an empty axis is 0
+    B2_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)(outer * inner) * dtype_size(dtype), st));
+    t_kernel = "row_memset";
+    return B2_OK;
+  }
+  const int rc = axis_reduce_launch(op, x, out, outer, R, inner, dtype, workspace, ws_bytes, st);
+  if (rc == B2_OK) t_kernel = "axis_reduce";
+  return rc;
+}
+
 size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t a3) {
   (void)a3;
   switch (kind) {
@@ -326,6 +366,7 @@ size_t b2_query_workspace(int kind, int64_t a0, int64_t a1, int64_t a2, int64_t 
       return gemm_f16_workspace(a0, a1, a2, B2_ACT_NONE);
     case 1: return row_op_workspace((int)a0, a1, a2);
     case 2: return 0;
+    case 3: return axis_reduce_workspace(a0, a1, a2);
     default: return 0;
   }
 }
