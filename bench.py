@@ -24,6 +24,7 @@ flushed by writing a 256 MB buffer between timed launches, outside the events.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -462,6 +463,8 @@ def run_b2(args, world, rank, local):
         barrier(world)
         st = torch.cuda.current_stream()
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        gc.collect()
+        gc.disable()  # no collector pause inside the host-paced e2e steps
         h0 = time.perf_counter()
         evs[0].record(st)
         for i in range(args.steps):
@@ -469,6 +472,7 @@ def run_b2(args, world, rank, local):
             evs[i + 1].record(st)
         host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         torch.cuda.synchronize()
+        gc.enable()
         barrier(world)
         step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
         e2e_per_rank = all_gather_floats(sum(step_ms) / args.steps, world)
