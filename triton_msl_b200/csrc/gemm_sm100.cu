@@ -817,9 +817,6 @@ size_t gemm_f16_workspace(long long M, long long N, long long K, int act) {
   return gemm_plan(M, N, K, act).ws;
 }
 
-int gemm_f16_plan_splits(long long M, long long N, long long K, int act) {
-  return gemm_plan(M, N, K, act).splits;
-}
 
 // Split-K plan of the 3xTF32 GEMM (one 128x256 tile per CTA): when the tiles
 // fill at most half the SMs (2048^3 has 64 tiles), the tripled K loop is split

@@ -1,7 +1,7 @@
 // Blackwell (sm_100a) building blocks in inline PTX: mbarriers with bounded
-// waits, TMA tile loads (each CTA loads its own tiles; no cross-CTA broadcast),
-// tcgen05 TMEM allocation / MMA / commit / load / store, and the shared-memory
-// matrix descriptors the tensor cores read.
+// waits, TMA tile loads (each load fills one CTA's own shared memory), tcgen05
+// TMEM allocation / MMA / commit / load / store for one CTA and for CTA pairs
+// (cta_group::2), and the shared-memory matrix descriptors the tensor cores read.
 //
 // Shared-memory operand layouts used here (byte offsets, 1024-byte aligned atoms):
 //  * K-major, 128-byte swizzle: rows of 64 fp16 (128 B) at a 128 B pitch,
