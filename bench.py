@@ -1,13 +1,13 @@
 #!/usr/bin/env python
 """Benchmark of the hot path (one JSON line on rank 0).
 
-Headline: FlashAttention forward, fp16, causal,
+Headline (benchmark configuration 2, workloads.FA_F16_CAUSAL): FlashAttention forward, fp16, causal,
 q/k/v [B=4, H=16, S=2048, D=128] ~ N(0,1)*0.5, TFLOP/s with causal FLOPs =
 2*B*H*S^2*D. The same run also measures, under "extra":
-  * the other BASELINE configs per rank (attention D=64/32, bf16, fp32;
+  * the other benchmark configurations per rank (attention D=64/32, bf16, fp32;
     GEMM 8192^3 fp16 + bias + ReLU and fp32 2048^3; the row family on
     X[65536, 4096] fp32), each with its roofline and, at N=1, its CPU baseline;
-  * BASELINE config 5 as fixed total problems split across the ranks
+  * benchmark configuration 5 as fixed total problems split across the ranks
     ("scale_fa", "scale_gemm", "scale_rows_*": strong scaling, per-rank times,
     efficiency against rank 0 timing the whole problem alone, and a sampled
     oracle check per rank).
@@ -543,7 +543,7 @@ def run_b2(args, world, rank, local):
 
 
 def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, threads, model):
-    """The other BASELINE configs (attention D=64/32, bf16, fp32; GEMM 8192^3 +
+    """The other benchmark configurations (attention D=64/32, bf16, fp32; GEMM 8192^3 +
     bias + ReLU and fp32 2048^3; the row family at 65536x4096), per-rank
     weak-scaling copies, same timing rules, each with its roofline, its own
     ncu traffic and (N=1, rank 0) its CPU baseline."""
@@ -631,7 +631,7 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
 
 
 def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, threads, model):
-    """BASELINE config 5 and the row family as fixed total problems split across
+    """benchmark configuration 5 and the row family as fixed total problems split across
     the ranks with no collective (strong scaling): FA bf16 causal [64,32,8192,128]
     by (batch, head), GEMM bf16 65536x16384x16384 by 128-row M-tiles (B built on
     every rank from one seed: a replicated local copy), rows 65536x4096 fp32

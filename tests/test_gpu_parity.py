@@ -63,7 +63,7 @@ def test_fa_long_sequence_bf16_causal(D):
 
 
 def test_fa_config1_fp32():
-    """fp32 non-causal [1,4,256,64], N(0,1) seed 0, scale 1/8."""
+    """benchmark configuration 1: fp32 non-causal [1,4,256,64], N(0,1) seed 0, scale 1/8."""
     q, k, v = W.fa_inputs(W.FA_F32, seed=0)
     o = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=False, sm_scale=1 / 8)
     assert b2.last_kernel() == "fa_simt"
@@ -234,7 +234,7 @@ def test_gemm_k_major_b_linear_layout():
 
 
 def test_gemm_config3_prime_fp32():
-    """fp32 inputs at 2048^3 (BASELINE config 3'), max-abs 1e-4, on the 3xTF32
+    """fp32 inputs at 2048^3 (benchmark configuration 3'), max-abs 1e-4, on the 3xTF32
     tensor-core path."""
     cfg = W.GEMM_F32
     a, b, _ = W.gemm_inputs(cfg, seed=0)
@@ -298,7 +298,7 @@ def test_gemm_tf32x3_error_growth_with_k(K):
     """The tensor core's fp32 accumulation loses about one unit in the last
     place of the running sum per K=8 step, so the error grows with K and with
     |C| (measured on B200: ~2.7e-5 of max|C| at K=2048, ~1.9e-4 at K=16384),
-    an order below plain TF32 and well inside 1e-4 for configs like BASELINE's
+    an order below plain TF32 and well inside 1e-4 for configs like the benchmark's
     (A, B ~ N(0,1)/sqrt(K), |C| ~ 0.02: 2.3e-6 at 2048^3). Bound written here:
     max-abs <= 5e-5 * (K / 2048) * max|C|."""
     a = _rand((256, K), torch.float32, 89)
@@ -335,7 +335,7 @@ def test_gemm_odd_strides_fall_back_to_cuda_cores():
 
 
 def test_gemm_config3_full_size_sampled():
-    """BASELINE config 3 at full size (8192^3 + bias + ReLU, fp16 out), checked on
+    """benchmark configuration 3 at full size (8192^3 + bias + ReLU, fp16 out), checked on
     sampled row blocks against the fp32 oracle."""
     cfg = W.GEMM_F16
     a, b, bias = W.gemm_inputs(cfg, device=DEV, seed=0)
@@ -427,7 +427,7 @@ def test_row_edge_shapes():
 
 
 def test_row_config4_full_size_properties():
-    """BASELINE config 4 at full size: sampled rows vs the oracle, plus
+    """benchmark configuration 4 at full size: sampled rows vs the oracle, plus
     size-independent properties over every row."""
     x, w, b = W.row_inputs(W.ROWS_F32, device=DEV, seed=0)
     idx = torch.tensor([0, 1, 4095, 32768, 65535])
@@ -452,7 +452,7 @@ def test_device_status_clean():
 
 @pytest.mark.parametrize("D", [128, 64, 32])
 def test_fa_config2_full_size_sampled(D):
-    """BASELINE config 2 at full size ([4,16,2048,D] fp16 causal, N(0,1)*0.5),
+    """benchmark configuration 2 at full size ([4,16,2048,D] fp16 causal, N(0,1)*0.5),
     checked on sampled (batch, head) slices against the oracle."""
     cfg = W.FAConfig("c2", 4, 16, 2048, D, True, torch.float16, 0.5)
     q, k, v = W.fa_inputs(cfg, device=DEV, seed=0)
@@ -465,7 +465,7 @@ def test_fa_config2_full_size_sampled(D):
 
 
 def test_fa_config5_full_size_sampled():
-    """BASELINE config 5 attention at full size ([64,32,8192,128] bf16 causal),
+    """benchmark configuration 5 attention at full size ([64,32,8192,128] bf16 causal),
     sampled heads against the oracle plus a finiteness check over all of O."""
     cfg = W.FA_BF16_SCALE
     g = torch.Generator(device=DEV).manual_seed(0)
@@ -481,7 +481,7 @@ def test_fa_config5_full_size_sampled():
 
 
 def test_gemm_config5_full_size_sampled():
-    """BASELINE config 5 GEMM at full size (65536 x 16384 x 16384 bf16), sampled
+    """benchmark configuration 5 GEMM at full size (65536 x 16384 x 16384 bf16), sampled
     row blocks against the fp32 oracle."""
     cfg = W.GEMM_BF16_SCALE
     a, b, _ = W.gemm_inputs(cfg, device=DEV, seed=0)

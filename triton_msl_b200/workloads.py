@@ -64,7 +64,11 @@ class RowConfig:
         return x + es * self.rows
 
 
-# BASELINE configs
+# Benchmark configurations of the hot path (numbered as in bench.py and the
+# tests): 1 FA fp32 [1,4,256,64]; 2 FA fp16 causal [4,16,2048,D], D = 128 / 64
+# / 32; 3 GEMM fp16 8192^3 + bias + ReLU, and 3' fp32 2048^3; 4 the row family
+# on X[65536, 4096] fp32; 5 the 8-GPU scale-out problems (FA bf16 causal
+# [64,32,8192,128], GEMM bf16 65536 x 16384 x 16384).
 FA_F32 = FAConfig("fa_f32_B1_H4_S256_D64", 1, 4, 256, 64, False, torch.float32)
 FA_F16_CAUSAL = FAConfig("fa_f16_causal_B4_H16_S2048_D128", 4, 16, 2048, 128, True,
                          torch.float16, 0.5)
