@@ -782,7 +782,11 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
         out[f"scale_rows_{op}"] = e
     # T(1): rank 0 alone on each whole problem, after every sharded measurement
     # (so the long single-GPU runs do not heat rank 0 ahead of its shard timings)
-    for key, build, fn_of in pending:
+    # lightest first (the rows), each after a 1 s idle pause so a whole-problem
+    # run does not start on a GPU still held down by the previous one's power draw
+    for key, build, fn_of in sorted(pending, key=lambda p: not p[0].startswith("scale_rows")):
+        barrier(world)
+        time.sleep(1.0)
         full = full_time(build, fn_of)
         e = out[key]
         e["full_problem_ms_1gpu"] = round(full, 4) if full else None
