@@ -11,17 +11,19 @@
 // Rows whose keys are all masked return 0 (reference oracle nan_to_num,
 // tests/test_flash_attention.py:124-135).
 //
-// Tiling: 64 query rows x 64 keys per step, 256 threads; thread (rg, cg) owns
-// rows 4*rg..4*rg+3 and columns cg + 16*j. Q, K, V, P staged in shared memory
-// as fp32 (padded rows, conflict-free).
+// Tiling: 16*RPT query rows x 64 keys per step, 256 threads; thread (rg, cg)
+// owns rows RPT*rg..RPT*rg+RPT-1 and columns cg + 16*j. RPT = 4 (64-row tiles)
+// normally; RPT = 1 (16-row tiles, four times the CTAs) when 64-row tiles would
+// leave most SMs idle (the fp32 [1,4,256,64] configuration: 64 CTAs instead of
+// 16). Q, K, V, P staged in shared memory as fp32 (padded rows, conflict-free).
 #include "b2_common.cuh"
 
 namespace b2 {
 namespace {
 
-constexpr int kBM = 64, kBN = 64, kThreads = 256;
+constexpr int kBN = 64, kThreads = 256;
 
-template <typename T, int DMAX>
+template <typename T, int DMAX, int RPT>
 __global__ void __launch_bounds__(kThreads)
 fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                T* __restrict__ o, int H, int S, int D, const long long* __restrict__ st_dev,
@@ -30,6 +32,7 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
                long long svz, long long svh, long long svn, long long svk,
                long long soz, long long soh, long long som, long long sok,
                float scale, int causal) {
+  constexpr int kBM = 16 * RPT;
   extern __shared__ float smem[];
   constexpr int DP = DMAX + 1;
   float* Qs = smem;                 // [kBM][DP]
@@ -52,16 +55,27 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   constexpr int NJ = DMAX / 16;
 
   // Stage q * scale (the reference scales q before the dot).
-  for (int idx = tid; idx < kBM * D; idx += kThreads) {
-    const int r = idx / D, d = idx % D;
-    const int m = m0 + r;
-    Qs[r * DP + d] = m < S ? to_f32<T>(qb[m * sqm + d * sqk]) * scale : 0.f;
+  {
+    constexpr int PQ = (kBM * DMAX + kThreads - 1) / kThreads;
+    float qr[PQ];
+#pragma unroll
+    for (int it = 0; it < PQ; ++it) {
+      const int idx = tid + it * kThreads;
+      const int r = idx / D, d = idx % D;
+      const int m = m0 + r;
+      qr[it] = (idx < kBM * D && m < S) ? to_f32<T>(qb[(long long)m * sqm + d * sqk]) * scale : 0.f;
+    }
+#pragma unroll
+    for (int it = 0; it < PQ; ++it) {
+      const int idx = tid + it * kThreads;
+      if (idx < kBM * D) Qs[(idx / D) * DP + idx % D] = qr[it];
+    }
   }
 
-  float acc[4][NJ];
-  float mrow[4], lrow[4];
+  float acc[RPT][NJ];
+  float mrow[RPT], lrow[RPT];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     mrow[i] = -INFINITY;
     lrow[i] = 0.f;
 #pragma unroll
@@ -70,37 +84,61 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 
   int hi = S;
   if (causal) hi = min(m0 + kBM, S);
-  for (int n0 = 0; n0 < hi; n0 += kBN) {
-    __syncthreads();
-    for (int idx = tid; idx < kBN * D; idx += kThreads) {
+  // K and V of the next block are loaded into registers while the current one
+  // is computed (all of a thread's elements in flight together), then stored to
+  // shared memory at the top of the next iteration.
+  constexpr int PER = kBN * DMAX / kThreads;
+  float kr[PER], vr[PER];
+  auto load_kv = [&](int nb) {
+#pragma unroll
+    for (int it = 0; it < PER; ++it) {
+      const int idx = tid + it * kThreads;
       const int r = idx / D, d = idx % D;
-      const int n = n0 + r;
-      const bool ok = n < S;
-      Ks[r * DP + d] = ok ? to_f32<T>(kb[n * skn + d * skk]) : 0.f;
-      Vs[r * DMAX + d] = ok ? to_f32<T>(vb[n * svn + d * svk]) : 0.f;
+      const int n = nb + r;
+      const bool ok = idx < kBN * D && n < S;
+      kr[it] = ok ? to_f32<T>(kb[(long long)n * skn + d * skk]) : 0.f;
+      vr[it] = ok ? to_f32<T>(vb[(long long)n * svn + d * svk]) : 0.f;
+    }
+  };
+  // (head dims up to 64; at 128 the second set of registers would spill, so
+  // the block's own loads are issued at the top of its iteration instead)
+  constexpr bool kPipe = DMAX <= 64;
+  if (kPipe && hi > 0) load_kv(0);
+  for (int n0 = 0; n0 < hi; n0 += kBN) {
+    if (!kPipe) load_kv(n0);
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < PER; ++it) {
+      const int idx = tid + it * kThreads;
+      if (idx < kBN * D) {
+        const int r = idx / D, d = idx % D;
+        Ks[r * DP + d] = kr[it];
+        Vs[r * DMAX + d] = vr[it];
+      }
     }
     __syncthreads();
+    if (kPipe && n0 + kBN < hi) load_kv(n0 + kBN);
 
-    float s[4][4];
+    float s[RPT][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
     for (int d = 0; d < D; ++d) {
-      float qv[4], kv[4];
+      float qv[RPT], kv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) qv[i] = Qs[(rg * 4 + i) * DP + d];
+      for (int i = 0; i < RPT; ++i) qv[i] = Qs[(rg * RPT + i) * DP + d];
 #pragma unroll
       for (int j = 0; j < 4; ++j) kv[j] = Ks[(cg + 16 * j) * DP + d];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
     }
 
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int m = m0 + rg * 4 + i;
+    for (int i = 0; i < RPT; ++i) {
+      const int m = m0 + rg * RPT + i;
       float tmax = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -118,7 +156,7 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       for (int j = 0; j < 4; ++j) {
         const float p = expf(s[i][j] - muse);
         psum += p;
-        Ps[(rg * 4 + i) * (kBN + 1) + cg + 16 * j] = p;
+        Ps[(rg * RPT + i) * (kBN + 1) + cg + 16 * j] = p;
       }
 #pragma unroll
       for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off, 16);
@@ -130,22 +168,22 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     __syncthreads();
     const int nlim = min(kBN, S - n0);
     for (int c = 0; c < nlim; ++c) {
-      float pv[4];
+      float pv[RPT];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pv[i] = Ps[(rg * 4 + i) * (kBN + 1) + c];
+      for (int i = 0; i < RPT; ++i) pv[i] = Ps[(rg * RPT + i) * (kBN + 1) + c];
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         const int d = cg + 16 * j;
         const float vv = Vs[c * DMAX + d];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i][j] = fmaf(pv[i], vv, acc[i][j]);
+        for (int i = 0; i < RPT; ++i) acc[i][j] = fmaf(pv[i], vv, acc[i][j]);
       }
     }
   }
 
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + rg * 4 + i;
+  for (int i = 0; i < RPT; ++i) {
+    const int m = m0 + rg * RPT + i;
     if (m >= S) continue;
     const float inv = lrow[i] > 0.f ? 1.f / lrow[i] : 0.f;
 #pragma unroll
@@ -156,11 +194,12 @@ fa_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   }
 }
 
-template <typename T, int DMAX>
-int launch_t(const void* q, const void* k, const void* v, void* o, long long B, long long H,
+template <typename T, int DMAX, int RPT>
+int launch_r(const void* q, const void* k, const void* v, void* o, long long B, long long H,
              long long S, long long D, const int64_t* s, float scale, int causal, cudaStream_t st) {
+  constexpr int kBM = 16 * RPT;
   const size_t smem = sizeof(float) * (kBM * (DMAX + 1) + kBN * (DMAX + 1) + kBN * DMAX + kBM * (kBN + 1));
-  auto kern = fa_simt_kernel<T, DMAX>;
+  auto kern = fa_simt_kernel<T, DMAX, RPT>;
   B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((unsigned)((S + kBM - 1) / kBM), (unsigned)(B * H));
   kern<<<grid, kThreads, smem, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, (int)H, (int)S,
@@ -169,6 +208,15 @@ int launch_t(const void* q, const void* k, const void* v, void* o, long long B, 
                                      scale, causal);
   B2_CHECK_LAUNCH();
   return B2_OK;
+}
+
+template <typename T, int DMAX>
+int launch_t(const void* q, const void* k, const void* v, void* o, long long B, long long H,
+             long long S, long long D, const int64_t* s, float scale, int causal, cudaStream_t st) {
+  const long long ctas64 = ((S + 63) / 64) * B * H;
+  if (ctas64 < device_sm_count())
+    return launch_r<T, DMAX, 1>(q, k, v, o, B, H, S, D, s, scale, causal, st);
+  return launch_r<T, DMAX, 4>(q, k, v, o, B, H, S, D, s, scale, causal, st);
 }
 
 template <typename T>
