@@ -626,7 +626,33 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
         if do_cpu:
             e["cpu_baseline"] = cpu_rows(r, op, cs, threads, model)
         out[f"{r.name}_{op}"] = e
+    # the same X reduced over its other axis (sum over rows: 4096 outputs)
+    fn = lambda: b2.reduce(x, "sum", 0)
+    fn()
+    kname = b2.last_kernel()
+    ms, per = time_one(fn, steps, 3, flush, world)
+    byt = r.rows * r.cols * 4 + r.cols * 4
+    gbs = byt / (ms / 1e3) / 1e9
+    out[f"{r.name}_sum_dim0"] = {
+        "value": round(world * gbs, 1), "unit": "GB/s", "ms": round(ms, 4),
+        "per_rank_ms": [round(x_, 4) for x_ in per], "kernel": kname,
+        "roofline": roofline(kname, gbs, float(peaks["hbm_gbs"]), "GB/s", "hbm",
+                             traffic.get(f"{r.name}_sum_dim0"), peak_kind + " copy")}
     del x, w, bb
+    # GEMM 8192^3 fp16 with a general epilogue chain (bias, scale, GELU, clamp)
+    a, bm, bias = W.gemm_inputs(g, device=dev, seed=rank)
+    chain = [("add_bias",), ("mul", 0.5), ("gelu",), ("clamp", -1.0, 4.0)]
+    fn = lambda: b2.gemm_epilogue(a, bm, chain, bias, torch.float16)
+    fn()
+    kname = b2.last_kernel()
+    ms, per = time_one(fn, steps, 3, flush, world)
+    ach = g.flops() / (ms / 1e3) / 1e12
+    out["gemm_f16_8192_epilogue_chain"] = {
+        "value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+        "per_rank_ms": [round(x_, 4) for x_ in per], "kernel": kname, "chain": [c[0] for c in chain],
+        "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor", None,
+                             peak_kind + " bf16 burst")}
+    del a, bm, bias
     return out
 
 

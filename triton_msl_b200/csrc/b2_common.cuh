@@ -137,6 +137,65 @@ __device__ __forceinline__ float epi_op(float x, int code, float a, float b, flo
   }
 }
 
+// A chain over N values of one output row chunk: one branch per op, then a
+// straight loop over the chunk (a per-element branch over 34 cases costs the
+// epilogue warps far more than the arithmetic).
+template <int N>
+__device__ __forceinline__ void epi_chain_chunk(float (&f)[N], const float (&bv)[N], const EpiProgram& p) {
+#define B2_EPI_CASE(CODE, EXPR)   \
+  case CODE:                      \
+    _Pragma("unroll")             \
+    for (int j = 0; j < N; ++j) { \
+      const float x = f[j];       \
+      (void)x;                    \
+      f[j] = (EXPR);              \
+    }                             \
+    break;
+#pragma unroll 1
+  for (int o = 0; o < p.n; ++o) {
+    const float a = p.a[o], b = p.b[o];
+    switch (p.code[o]) {
+      B2_EPI_CASE(B2_EPI_ADD, x + a)
+      B2_EPI_CASE(B2_EPI_SUB, x - a)
+      B2_EPI_CASE(B2_EPI_RSUB, a - x)
+      B2_EPI_CASE(B2_EPI_MUL, x * a)
+      B2_EPI_CASE(B2_EPI_DIV, x / a)
+      B2_EPI_CASE(B2_EPI_RDIV, a / x)
+      B2_EPI_CASE(B2_EPI_ADD_BIAS, x + bv[j])
+      B2_EPI_CASE(B2_EPI_MUL_BIAS, x * bv[j])
+      B2_EPI_CASE(B2_EPI_FMA, fmaf(x, a, b))
+      B2_EPI_CASE(B2_EPI_RELU, apply_act(x, B2_ACT_RELU))
+      B2_EPI_CASE(B2_EPI_GELU, apply_act(x, B2_ACT_GELU))
+      B2_EPI_CASE(B2_EPI_GELU_TANH, apply_act(x, B2_ACT_GELU_TANH))
+      B2_EPI_CASE(B2_EPI_CLAMP, x != x ? x : fminf(fmaxf(x, a), b))
+      B2_EPI_CASE(B2_EPI_CLAMPNUM, fminf(fmaxf(x, a), b))
+      B2_EPI_CASE(B2_EPI_MAX, (x != x || a != a) ? __int_as_float(0x7fffffff) : fmaxf(x, a))
+      B2_EPI_CASE(B2_EPI_MIN, (x != x || a != a) ? __int_as_float(0x7fffffff) : fminf(x, a))
+      B2_EPI_CASE(B2_EPI_MAXNUM, fmaxf(x, a))
+      B2_EPI_CASE(B2_EPI_MINNUM, fminf(x, a))
+      B2_EPI_CASE(B2_EPI_NEG, -x)
+      B2_EPI_CASE(B2_EPI_EXP, expf(x))
+      B2_EPI_CASE(B2_EPI_EXP2, exp2f(x))
+      B2_EPI_CASE(B2_EPI_LOG, logf(x))
+      B2_EPI_CASE(B2_EPI_LOG2, log2f(x))
+      B2_EPI_CASE(B2_EPI_SQRT, sqrtf(x))
+      B2_EPI_CASE(B2_EPI_RSQRT, rsqrtf(x))
+      B2_EPI_CASE(B2_EPI_SIN, sinf(x))
+      B2_EPI_CASE(B2_EPI_COS, cosf(x))
+      B2_EPI_CASE(B2_EPI_ERF, erff(x))
+      B2_EPI_CASE(B2_EPI_TANH, tanhf(x))
+      B2_EPI_CASE(B2_EPI_FLOOR, floorf(x))
+      B2_EPI_CASE(B2_EPI_CEIL, ceilf(x))
+      B2_EPI_CASE(B2_EPI_ABS, fabsf(x))
+      B2_EPI_CASE(B2_EPI_SILU, x / (1.f + expf(-x)))
+      B2_EPI_CASE(B2_EPI_SIGMOID, 1.f / (1.f + expf(-x)))
+      default:
+        break;
+    }
+  }
+#undef B2_EPI_CASE
+}
+
 __device__ __forceinline__ float epi_chain(float x, float bias, const EpiProgram& p) {
 #pragma unroll 1
   for (int o = 0; o < p.n; ++o) x = epi_op(x, p.code[o], p.a[o], p.b[o], bias);

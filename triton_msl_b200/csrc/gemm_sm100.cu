@@ -375,8 +375,9 @@ gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           case B2_ACT_GELU_TANH: act_chunk<B2_ACT_GELU_TANH>(f, r, bv, alpha); break;
           case B2_ACT_SILU: act_chunk<B2_ACT_SILU>(f, r, bv, alpha); break;
           case kActChain:
-#pragma unroll 4
-            for (int j = 0; j < 32; ++j) f[j] = epi_chain(__uint_as_float(r[j]) * alpha, bv[j], prog);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * alpha;
+            epi_chain_chunk<32>(f, bv, prog);
             break;
           default: act_chunk<B2_ACT_NONE>(f, r, bv, alpha); break;
         }

@@ -285,8 +285,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           case B2_ACT_GELU_TANH: pair_act_chunk<B2_ACT_GELU_TANH>(f, r, bv, alpha); break;
           case B2_ACT_SILU: pair_act_chunk<B2_ACT_SILU>(f, r, bv, alpha); break;
           case kActChain:
-#pragma unroll 4
-            for (int j = 0; j < 32; ++j) f[j] = epi_chain(__uint_as_float(r[j]) * alpha, bv[j], prog);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) * alpha;
+            epi_chain_chunk<32>(f, bv, prog);
             break;
           default: pair_act_chunk<B2_ACT_NONE>(f, r, bv, alpha); break;
         }

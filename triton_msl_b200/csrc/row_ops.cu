@@ -671,6 +671,8 @@ axis_reduce_kernel(const T* __restrict__ x, long long outer, long long R, long l
       idx[e] = 0x7fffffffffffffffLL;
     }
     const T* xo = x + o * R * inner + i0;
+    // unrolled so several rows' loads are in flight per thread
+#pragma unroll 8
     for (long long r = r0; r < r1; ++r) {
       float f[VEC];
       if constexpr (VEC == 4 && sizeof(T) == 4) {
@@ -750,12 +752,14 @@ AxisPlan axis_plan(long long outer, long long R, long long inner, bool vec4) {
   p.vec = vec4 ? 4 : 1;
   p.xblocks = (inner + 256LL * p.vec - 1) / (256LL * p.vec);
   const long long blocks = p.xblocks * outer;
-  const long long want = 2LL * num_sms();
+  // enough CTAs for every SM to hold several (memory-level parallelism), each
+  // still reading at least 128 rows
+  const long long want = 4LL * num_sms();
   long long sp = 1;
   if (blocks < want && R >= 256) {
     sp = (want + blocks - 1) / blocks;
     if (sp > R / 128) sp = R / 128;
-    if (sp > 64) sp = 64;
+    if (sp > 256) sp = 256;
     if (sp < 1) sp = 1;
   }
   p.r_chunk = (R + sp - 1) / sp;
