@@ -644,6 +644,10 @@ int dispatch_type(int op, const void* x, const void* w, const void* b, void* out
 }
 
 // ------------------------------------------------ reduction over a middle axis
+// rows unrolled per thread, and target CTAs per SM (measured on B200 for
+// sum over dim 0 of [65536, 4096] and dim 1 of [16, 4096, 4096]: 4-16 rows and
+// 4 CTAs/SM within 2 %, 8 CTAs/SM 10-20 % slower)
+constexpr int kAxisUnroll = 8, kAxisWant = 4;
 // x[outer, R, inner] (contiguous) -> out[outer, inner], reducing over R
 // (torch's sum / amax / amin / argmax / argmin along a dim that is not the last:
 // the reference fuzzer's 2d_sum_ax0 / 3d_sum_ax0 forms, tests/test_fuzz_reduce.py:88-139).
@@ -672,7 +676,7 @@ axis_reduce_kernel(const T* __restrict__ x, long long outer, long long R, long l
     }
     const T* xo = x + o * R * inner + i0;
     // unrolled so several rows' loads are in flight per thread
-#pragma unroll 8
+#pragma unroll kAxisUnroll
     for (long long r = r0; r < r1; ++r) {
       float f[VEC];
       if constexpr (VEC == 4 && sizeof(T) == 4) {
@@ -754,7 +758,7 @@ AxisPlan axis_plan(long long outer, long long R, long long inner, bool vec4) {
   const long long blocks = p.xblocks * outer;
   // enough CTAs for every SM to hold several (memory-level parallelism), each
   // still reading at least 128 rows
-  const long long want = 4LL * num_sms();
+  const long long want = (long long)kAxisWant * num_sms();
   long long sp = 1;
   if (blocks < want && R >= 256) {
     sp = (want + blocks - 1) / blocks;
