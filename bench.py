@@ -822,7 +822,7 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
 
 ONLY = ("headline", "fa_d64", "fa_d32", "fa_bf16", "fa_f32", "gemm_f16", "gemm_f32",
         "rows_softmax", "rows_layernorm", "rows_rmsnorm", "rows_sum", "rows_max", "rows_argmax",
-        "gemm_bf16_scale_shard")
+        "gemm_bf16_scale_shard", "rows_sum_dim0", "gemm_f16_chain")
 
 
 def run_only(args):
@@ -845,6 +845,17 @@ def run_only(args):
         fn = (lambda: b2.gemm(a, bm, bias, "relu", torch.float16)) if name == "gemm_f16" \
             else (lambda: b2.gemm(a, bm))
         work, unit = cfg.flops(), "TFLOP/s"
+    elif name == "gemm_f16_chain":
+        cfg = W.GEMM_F16
+        a, bm, bias = W.gemm_inputs(cfg, device=dev)
+        chain = [("add_bias",), ("mul", 0.5), ("gelu",), ("clamp", -1.0, 4.0)]
+        fn = lambda: b2.gemm_epilogue(a, bm, chain, bias, torch.float16)
+        work, unit = cfg.flops(), "TFLOP/s"
+    elif name == "rows_sum_dim0":
+        r = W.ROWS_F32
+        x, _, _ = W.row_inputs(r, device=dev)
+        fn = lambda: b2.reduce(x, "sum", 0)
+        work, unit = r.rows * r.cols * 4 + r.cols * 4, "GB/s"
     elif name == "gemm_bf16_scale_shard":
         cfg = W.GEMM_BF16_SCALE
         a = torch.randn(8192, cfg.K, device=dev).to(cfg.dtype)
