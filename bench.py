@@ -650,7 +650,8 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
     out["gemm_f16_8192_epilogue_chain"] = {
         "value": round(world * ach, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
         "per_rank_ms": [round(x_, 4) for x_ in per], "kernel": kname, "chain": [c[0] for c in chain],
-        "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor", None,
+        "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor",
+                             traffic.get("gemm_f16_8192_epilogue_chain"),
                              peak_kind + " bf16 burst")}
     del a, bm, bias
     return out
