@@ -38,9 +38,13 @@ constexpr uint32_t kBBytes = kHalf * kBK * 2;  // 16 KB: this CTA's B columns
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 2 * kBN;
 #ifndef B2_GEMM_PAIR_GROUP_M
-#define B2_GEMM_PAIR_GROUP_M 16
+#define B2_GEMM_PAIR_GROUP_M 8
 #endif
-constexpr int kGroupM = B2_GEMM_PAIR_GROUP_M;  // raster: 256-row blocks per group
+// raster: 256-row blocks per group. Measured on 8192^3 (DRAM read bytes / TFLOP/s):
+// 4: 1.73 GB / 1297, 8: 1.10 / 1384, 16: 1.23 / 1378, 32 and 64: 2.32 / 1265 --
+// 74 concurrent pair tiles keep a ~9 x 8 window (A rows + B columns, ~70 MB at
+// K = 8192) hottest in L2 with 8.
+constexpr int kGroupM = B2_GEMM_PAIR_GROUP_M;
 
 template <typename TO> struct PairCfg {
   static constexpr int kRing = sizeof(TO) == 4 ? 5 : 6;
