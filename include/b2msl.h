@@ -153,7 +153,8 @@ int b2_fa_fwd(const void* q, const void* k, const void* v, void* o,
  * measured 2.5e-5 * max|C| at K=2048); with no workspace, fp32 FMA.
  * fp16/bf16 inputs: shapes with at least one full wave of 256x256 output
  * tiles and at most 4e12 FLOP run on CTA pairs (two SMs per tile, M=256
- * tensor-core MMAs); the others on one SM per 128x256 or 128x128 tile,
+ * tensor-core MMAs; a last wave that fills at most half of the pairs runs as
+ * 256x128 half tiles); the others on one SM per 128x256 or 128x128 tile,
  * whichever leaves fewer SMs idle for the work; when even narrow tiles would fill at most half the SMs and K >= 512,
  * the K loop is split across CTAs (split-K) given the workspace
  * b2_query_workspace reports, with fp32 partial sums reduced in a fixed order

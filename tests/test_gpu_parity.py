@@ -191,6 +191,45 @@ def test_gemm_pair_paths(M, N, K, b_kmajor, act, out_dtype, dtype):
     assert b2.device_status(0) == 0
 
 
+# Pair launches whose last wave fills at most half the pairs compute those
+# tiles as two 256 x 128 halves on two pairs (4096^3: 256 tiles on 74 pairs,
+# the 34 left over in halves; 1024 x 5888: 18 left over). Both B layouts and
+# ragged M/N/K (the last column tile's second half only partly inside N).
+@pytest.mark.parametrize("M,N,K,b_kmajor,out_dtype", [
+    (4096, 4096, 4096, False, torch.float16),
+    (1024, 5888, 2048, True, torch.bfloat16),
+    (1000, 5800, 2104, False, torch.float32),
+    (1000, 5800, 2104, True, torch.float16),
+])
+def test_gemm_pair_last_wave_halves(M, N, K, b_kmajor, out_dtype):
+    dtype = torch.bfloat16 if out_dtype == torch.bfloat16 else torch.float16
+    a = _rand((M, K), dtype, 95, 1 / math.sqrt(K))
+    bias = _rand((N,), torch.float32, 97, 0.1)
+    if b_kmajor:
+        w = _rand((N, K), dtype, 96, 1 / math.sqrt(K))
+        b, bd = w.t(), w.to(DEV).t()
+    else:
+        b = _rand((K, N), dtype, 96, 1 / math.sqrt(K))
+        bd = b.to(DEV)
+    c = b2.gemm(a.to(DEV), bd, bias.to(DEV), "relu", out_dtype)
+    assert b2.last_kernel() == "gemm_sm100_pair"
+    _check(c, O.ref_gemm(a, b, bias, "relu", torch.float32), dtype)
+    assert b2.device_status(0) == 0
+
+
+def test_gemm_epilogue_chain_on_pair_halves():
+    """The general epilogue chain on a pair launch whose last wave runs in halves."""
+    M, N, K = 2304, 2304, 2048  # 81 tiles on 74 pairs: 7 left over, in halves
+    a = _rand((M, K), torch.float16, 98, 1 / math.sqrt(K))
+    b = _rand((K, N), torch.float16, 99, 1 / math.sqrt(K))
+    bias = _rand((N,), torch.float32, 100, 0.1)
+    chain = [("add_bias",), ("mul", 1.5), ("add", -0.25), ("tanh",), ("clamp", -0.5, 0.75)]
+    c = b2.gemm_epilogue(a.to(DEV), b.to(DEV), chain, bias.to(DEV), torch.float32)
+    assert b2.last_kernel() == "gemm_sm100_pair"
+    ref = O.ref_gemm_epilogue(a, b, chain, bias, torch.float32)
+    _check(c, ref, torch.float16)
+
+
 @pytest.mark.parametrize("act", ["none", "relu", "gelu", "silu"])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32, torch.bfloat16])
 def test_gemm_splitk_epilogue_and_k_major_b(act, out_dtype):

@@ -16,6 +16,10 @@
 //    and its four epilogue warps store them (alpha, bias, activation, cast,
 //    swizzled staging, TMA tensor stores) and report to rank 0's
 //    accumulator-free barrier.
+// Last wave: when the tiles left over after the full waves fill at most half
+// of the pairs, each of them is computed as two 256 x 128 halves on two pairs
+// (M=256, N=128 MMAs; each CTA loads 64 columns of B), so the last wave runs
+// about half as long; no partial sums, so no reduction or workspace.
 // Every wait is bounded (sm100.cuh); the CTAs meet at a cluster barrier before
 // the TMEM is freed.
 #include <cstdlib>
@@ -78,6 +82,19 @@ __device__ __forceinline__ void pair_tile_coords(int t, int num_m, int num_n, in
   nb = r / gsize;
 }
 
+// Work unit u of the persistent loop: whole tile u below tail_start, else
+// half (u - tail_start) & 1 (columns 0-127 or 128-255) of tile
+// tail_start + (u - tail_start) / 2.
+__device__ __forceinline__ void pair_unit(int u, int tail_start, int& t, int& half) {
+  if (u < tail_start) {
+    t = u;
+    half = -1;
+  } else {
+    t = tail_start + ((u - tail_start) >> 1);
+    half = (u - tail_start) & 1;
+  }
+}
+
 template <int ACT>
 __device__ __forceinline__ void pair_act_chunk(float (&f)[32], const uint32_t (&r)[32], const float* bv,
                                                float alpha) {
@@ -88,8 +105,9 @@ __device__ __forceinline__ void pair_act_chunk(float (&f)[32], const uint32_t (&
 template <typename TO, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmC, const void* __restrict__ bias, int bias_dt,
-                 int M, int N, int K, float alpha, int act, uint32_t idesc, const EpiProgram prog) {
+                 const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmC,
+                 const void* __restrict__ bias, int bias_dt, int M, int N, int K, float alpha, int act,
+                 uint32_t idesc, uint32_t idesc_half, int tail_start, const EpiProgram prog) {
   constexpr int kRing = PairCfg<TO>::kRing;
   constexpr uint32_t kStageOutBytes = PairCfg<TO>::kOutBytes;
   extern __shared__ uint8_t smem_raw[];
@@ -105,6 +123,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int num_m = (M + kPM - 1) / kPM, num_n = (N + kBN - 1) / kBN;
   const int tiles = num_m * num_n;
+  const int units = tail_start + 2 * (tiles - tail_start);
   const int nk = (K + kBK - 1) / kBK;
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -122,6 +141,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (!B_MN) tma_prefetch_desc(&tmBh);
     tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
@@ -142,24 +162,27 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       uint32_t phase = 0;
       uint32_t filled = 0;
       bool ok = true;
-      for (int t = pair; t < tiles && ok; t += npairs) {
-        int mb, nb;
+      for (int u = pair; u < units && ok; u += npairs) {
+        int t, half, mb, nb;
+        pair_unit(u, tail_start, t, half);
         pair_tile_coords(t, num_m, num_n, mb, nb);
+        // this CTA's B columns: 128 of the tile, or 64 of the tile's half
+        const int bcols = half < 0 ? kHalf : kHalf / 2;
+        const int bcol0 = nb * kBN + (half < 0 ? rank * kHalf : half * kHalf + rank * (kHalf / 2));
+        const uint32_t stage_tx = 2 * (kABytes + (uint32_t)bcols * kBK * 2);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, &g_pair_status, DEV_TIMEOUT_SLOT)) {
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * kStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], stage_tx);
           const uint32_t fb = full0 + stage * 8;
           tma_load_2d_pair(sA + stage * kABytes, &tmA, fb, kb * kBK, mb * kPM + rank * kHalf);
           if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < kHalf / 64; ++j)
-              tma_load_2d_pair(sB + stage * kBBytes + j * (64 * kBK * 2), &tmB, fb,
-                               nb * kBN + rank * kHalf + j * 64, kb * kBK);
+            for (int j = 0; j < bcols / 64; ++j)
+              tma_load_2d_pair(sB + stage * kBBytes + j * (64 * kBK * 2), &tmB, fb, bcol0 + j * 64, kb * kBK);
           } else {
-            tma_load_2d_pair(sB + stage * kBBytes, &tmB, fb, kb * kBK, nb * kBN + rank * kHalf);
+            tma_load_2d_pair(sB + stage * kBBytes, half < 0 ? &tmB : &tmBh, fb, kb * kBK, bcol0);
           }
           filled |= 1u << stage;
           if (++stage == kRing) {
@@ -193,7 +216,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, issued = false;
-      for (int t = pair; t < tiles && ok; t += npairs) {
+      for (int u = pair; u < units && ok; u += npairs) {
+        const uint32_t id = u < tail_start ? idesc : idesc_half;
         if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1u, abort_flag, &g_pair_status, DEV_TIMEOUT_EPI)) {
           ok = false;
           break;
@@ -213,7 +237,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const uint64_t ad = sdesc(a0 + k * 32, 16, 1024, kSwizzle128);
             const uint64_t bd = B_MN ? sdesc(b0 + k * 16 * 128, 64 * kBK * 2, 1024, kSwizzle128)
                                      : sdesc(b0 + k * 32, 16, 1024, kSwizzle128);
-            if (leader) mma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (leader) mma_f16_ss_pair(d_tmem, ad, bd, id, (kb | k) != 0 ? 1u : 0u);
           }
           issued = true;
           if (leader) mma_commit_pair(&bars->empty[stage], 0x3);
@@ -247,9 +271,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     int acc = 0;
     uint32_t acc_phase = 0;
     int tile_iter = 0;
-    for (int t = pair; t < tiles; t += npairs) {
-      int mb, nb;
+    for (int u = pair; u < units; u += npairs) {
+      int t, half, mb, nb;
+      pair_unit(u, tail_start, t, half);
       pair_tile_coords(t, num_m, num_n, mb, nb);
+      const int col0 = half < 0 ? 0 : half * kHalf;  // first tile column of this unit
+      const int nchunks = half < 0 ? kBN / 32 : kHalf / 32;
       float* tb_bias = sBias + (tile_iter & 1) * kBN;
       if (bias != nullptr) {
         const int et = threadIdx.x - 64;
@@ -265,17 +292,17 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const int row0 = mb * kPM + rank * kHalf + quarter * 32;
       const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * kBN;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < nchunks; ++c) {
         uint32_t r[32];
         tmem_ld32(tbase + c * 32, r);
         tmem_ld_wait();
-        const int n0 = nb * kBN + c * 32;
+        const int n0 = nb * kBN + col0 + c * 32;
         if (n0 >= N) continue;  // warp-uniform
         float bv[32];
         if (bias != nullptr) {
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
-            const float4 q = *reinterpret_cast<const float4*>(tb_bias + c * 32 + 4 * v);
+            const float4 q = *reinterpret_cast<const float4*>(tb_bias + col0 + c * 32 + 4 * v);
             bv[4 * v] = q.x; bv[4 * v + 1] = q.y; bv[4 * v + 2] = q.z; bv[4 * v + 3] = q.w;
           }
         } else {
@@ -339,10 +366,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   }
 }
 
+// B2MSL_GEMM_PAIR_HALVES=0 (read once) keeps the last wave in whole tiles: a
+// tuning and diagnostic override, unset in normal use.
+bool pair_halves_off() {
+  static const bool off = [] {
+    const char* e = getenv("B2MSL_GEMM_PAIR_HALVES");
+    return e != nullptr && !strcmp(e, "0");
+  }();
+  return off;
+}
+
 template <typename TO, bool B_MN>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const void* bias,
-                int bias_dt, long long M, long long N, long long K, float alpha, int act, uint32_t idesc,
-                cudaStream_t st) {
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbh, const CUtensorMap& tc,
+                const void* bias, int bias_dt, long long M, long long N, long long K, float alpha, int act,
+                uint32_t idesc, uint32_t idesc_half, cudaStream_t st) {
   auto kern = gemm_pair_kernel<TO, B_MN>;
   constexpr size_t smem = 1024 + PairCfg<TO>::kRing * kStageBytes + PairCfg<TO>::kEpiSmem + sizeof(PairBarriers);
   static_assert(smem <= 227 * 1024, "shared memory per CTA exceeded");
@@ -350,8 +387,12 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int sms = device_sm_count();
   const long long tiles = ((M + kPM - 1) / kPM) * ((N + kBN - 1) / kBN);
   const long long pairs = tiles < sms / 2 ? tiles : sms / 2;
-  kern<<<(unsigned)(2 * pairs), kThreads, smem, st>>>(ta, tb, tc, bias, bias_dt, (int)M, (int)N, (int)K, alpha,
-                                                      act, idesc, epi_program());
+  // last wave in halves when it fills at most half of the pairs
+  const long long rem = tiles % pairs;
+  const long long tail_start = (rem > 0 && 2 * rem <= pairs && !pair_halves_off()) ? tiles - rem : tiles;
+  kern<<<(unsigned)(2 * pairs), kThreads, smem, st>>>(ta, tb, tbh, tc, bias, bias_dt, (int)M, (int)N, (int)K,
+                                                      alpha, act, idesc, idesc_half, (int)tail_start,
+                                                      epi_program());
   B2_CHECK_LAUNCH();
   return B2_OK;
 }
@@ -381,7 +422,7 @@ int gemm_pair_launch(const void* A, const void* B, const void* bias, void* C, lo
                      cudaStream_t st) {
   const CUtensorMapDataType tdt =
       in_dt == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb, tbh, tc;
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)s[0] * 2};
@@ -399,7 +440,10 @@ int gemm_pair_launch(const void* A, const void* B, const void* bias, void* C, lo
     const uint64_t strides[1] = {(uint64_t)s[3] * 2};
     const uint32_t box[2] = {kBK, kHalf};
     if (!encode_tmap(&tb, tdt, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
+    const uint32_t box_half[2] = {kBK, kHalf / 2};  // 64 columns of B per CTA in a half tile
+    if (!encode_tmap(&tbh, tdt, 2, B, dims, strides, box_half, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ELAUNCH;
   }
+  if (b_mn) tbh = tb;
   {
     const int osz = dtype_size(out_dt);
     const CUtensorMapDataType cdt = out_dt == B2_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -413,17 +457,18 @@ int gemm_pair_launch(const void* A, const void* B, const void* bias, void* C, lo
       return B2_ELAUNCH;
   }
   const uint32_t idesc = idesc_f16(kPM, kBN, in_dt == B2_BF16, false, b_mn);
+  const uint32_t idesc_half = idesc_f16(kPM, kBN / 2, in_dt == B2_BF16, false, b_mn);
   if (bias == nullptr) bias_dt = B2_F32;
   switch (out_dt) {
     case B2_F16:
-      return b_mn ? launch_pair<__half, true>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st)
-                  : launch_pair<__half, false>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st);
+      return b_mn ? launch_pair<__half, true>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st)
+                  : launch_pair<__half, false>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st);
     case B2_BF16:
-      return b_mn ? launch_pair<__nv_bfloat16, true>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st)
-                  : launch_pair<__nv_bfloat16, false>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st);
+      return b_mn ? launch_pair<__nv_bfloat16, true>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st)
+                  : launch_pair<__nv_bfloat16, false>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st);
     case B2_F32:
-      return b_mn ? launch_pair<float, true>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st)
-                  : launch_pair<float, false>(ta, tb, tc, bias, bias_dt, M, N, K, alpha, act, idesc, st);
+      return b_mn ? launch_pair<float, true>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st)
+                  : launch_pair<float, false>(ta, tb, tbh, tc, bias, bias_dt, M, N, K, alpha, act, idesc, idesc_half, st);
   }
   set_error("b2_gemm: unsupported out dtype %d", out_dt);
   return B2_EINVAL;
