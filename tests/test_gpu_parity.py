@@ -572,6 +572,23 @@ def test_fa_host_pipeline_matches_device_path(causal, chunks):
     _check(o, O.ref_attention(q, k, v, causal), torch.float16)
 
 
+def test_fa_host_pipeline_back_to_back_calls_reuse_staging():
+    """Calls queued without synchronising, with inputs that grow and shrink: the
+    two device staging slots are reused (and regrown) only after the call that
+    last used them has read its output back, so every output is intact."""
+    shapes = [(1, 4, 256, 64), (2, 6, 300, 64), (1, 3, 128, 128), (2, 8, 512, 64), (1, 2, 64, 32),
+              (2, 8, 512, 64), (1, 4, 256, 64)]
+    cases = []
+    for i, shp in enumerate(shapes):
+        q, k, v = (_rand(shp, torch.float16, 200 + 3 * i + s, 0.5).pin_memory() for s in range(3))
+        cases.append((q, k, v, b2.flash_attn_fwd_host(q, k, v, causal=bool(i & 1), chunks=3)))
+    torch.cuda.synchronize()
+    for i, (q, k, v, o) in enumerate(cases):
+        ref = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=bool(i & 1)).cpu()
+        assert torch.equal(o, ref), f"call {i}"
+    b2.host_pipeline.release_staging()
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [32, 64, 128])
 @pytest.mark.parametrize("causal", [False, True])

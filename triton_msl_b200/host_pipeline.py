@@ -41,6 +41,48 @@ def _streams(dev: torch.device):
     return s
 
 
+class _Slot:
+    """Device staging for one call: q, k, v and o back to back, reused by later
+    calls once the event recorded after the call's last read-back has passed."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+        self.done: Optional[torch.cuda.Event] = None
+
+
+# Two staging slots per (host thread, device), used in turn, so a call's
+# host->device copies can start while the previous call's read-back drains.
+_STAGING: Dict[Tuple[int, int], list] = {}
+
+
+def _slot(dev: torch.device, nbytes: int) -> _Slot:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (threading.get_ident(), idx)
+    with _STREAMS_LOCK:
+        st = _STAGING.get(key)
+        if st is None:
+            st = _STAGING[key] = [0, _Slot(), _Slot()]
+    st[0] ^= 1
+    slot = st[1 + st[0]]
+    if slot.buf is None or slot.buf.numel() < nbytes:
+        if slot.done is not None:
+            slot.done.synchronize()  # the old buffer's last reader has finished
+        slot.buf = None
+        slot.buf = torch.empty((nbytes,), dtype=torch.uint8, device=dev)
+    return slot
+
+
+def release_staging() -> None:
+    """Drop this thread's device staging buffers (they are kept between calls)."""
+    me = threading.get_ident()
+    with _STREAMS_LOCK:
+        for key in [k for k in _STAGING if k[0] == me]:
+            for slot in _STAGING[key][1:]:
+                if slot.done is not None:
+                    slot.done.synchronize()
+            del _STAGING[key]
+
+
 def flash_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                         sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                         chunks: int = 4, device: Optional[torch.device] = None) -> torch.Tensor:
@@ -80,15 +122,16 @@ def flash_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     cur = torch.cuda.current_stream(dev)
     n = max(1, min(int(chunks), BH))
     bounds = [(BH * c) // n for c in range(n + 1)]
+    elems = BH * S * D
     with torch.cuda.device(dev):
-        # the copies may not start before earlier work on the caller's stream
+        slot = _slot(dev, 4 * elems * q.element_size())
+        dq, dk, dv, do = slot.buf[:4 * elems * q.element_size()].view(q.dtype).view(4, BH, S, D).unbind(0)
+        # the copies may not start before earlier work on the caller's stream,
+        # nor overwrite the slot before its previous call's last read-back
         s_in.wait_stream(cur)
         s_out.wait_stream(cur)
-        dq, dk, dv = (torch.empty((BH, S, D), dtype=q.dtype, device=dev) for _ in range(3))
-        for t in (dq, dk, dv):
-            t.record_stream(s_in)
-            t.record_stream(s_comp)
-        last = None
+        if slot.done is not None:
+            s_in.wait_event(slot.done)
         # All host->device copies are queued first, so the copy engine never waits
         # for the host to issue the next chunk's copies.
         ev_in = []
@@ -100,22 +143,21 @@ def flash_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
                 ev = torch.cuda.Event()
                 ev.record(s_in)
                 ev_in.append(ev)
+        comp_handle = s_comp.cuda_stream
         for c in range(n):
             h0, h1 = bounds[c], bounds[c + 1]
             if h1 == h0:
                 continue
             s_comp.wait_event(ev_in[c])
-            with torch.cuda.stream(s_comp):
-                o = ops.flash_attn_fwd(dq[h0:h1].unsqueeze(0), dk[h0:h1].unsqueeze(0),
-                                       dv[h0:h1].unsqueeze(0), causal, sm_scale)
-                ev_c = torch.cuda.Event()
-                ev_c.record(s_comp)
-            o.record_stream(s_out)
+            ops._fa_into(dq[h0:h1].unsqueeze(0), dk[h0:h1].unsqueeze(0), dv[h0:h1].unsqueeze(0),
+                         do[h0:h1].unsqueeze(0), causal, sm_scale, comp_handle)
+            ev_c = torch.cuda.Event()
+            ev_c.record(s_comp)
             s_out.wait_event(ev_c)
             with torch.cuda.stream(s_out):
-                of[h0:h1].copy_(o[0], non_blocking=True)
-                last = torch.cuda.Event()
-                last.record(s_out)
-        if last is not None:
-            cur.wait_event(last)
+                of[h0:h1].copy_(do[h0:h1], non_blocking=True)
+        last = torch.cuda.Event()
+        last.record(s_out)
+        slot.done = last
+        cur.wait_event(last)
     return out

@@ -64,16 +64,22 @@ def _fa_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,
                          f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
     if not (q.dtype == k.dtype == v.dtype):
         raise TypeError(f"{what}: q, k, v must share a dtype")
-    dt = _dtype_code(q, what)
+    o = torch.empty(tuple(q.shape), dtype=q.dtype, device=dev)
+    _fa_into(q, k, v, o, causal, sm_scale, _stream(dev))
+    return o
+
+
+def _fa_into(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, causal: bool,
+             sm_scale: float, stream: int) -> None:
+    """b2_fa_fwd into a caller-owned o (same shape as q) on the CUDA stream handle `stream`."""
+    dt = _dtype_code(q, "flash_attn_fwd")
     B, H, S, D = q.shape
-    o = torch.empty((B, H, S, D), dtype=q.dtype, device=dev)
     strides = [*q.stride(), *k.stride(), *v.stride(), *o.stride()]
-    with torch.cuda.device(dev):
+    with torch.cuda.device(q.device):
         st = _lib.lib().b2_fa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                                   B, H, S, D, _lib.i64_array(strides), float(sm_scale),
-                                  1 if causal else 0, dt, _stream(dev))
+                                  1 if causal else 0, dt, stream)
     _lib.check("b2_fa_fwd", st)
-    return o
 
 
 @torch.library.custom_op("b2msl::flash_attn_fwd", mutates_args=())
