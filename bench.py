@@ -450,12 +450,14 @@ def run_b2(args, world, rank, local):
 
         # e2e through the public host-tensor entry point: every step copies q, k, v
         # from pinned host memory, runs the kernel and reads o back, chunk-pipelined
-        # over (batch, head) on three streams (copies both ways overlap the kernel)
+        # over (batch, head) on three streams (copies both ways overlap the kernel;
+        # the inputs are CPU-prepared, so a step's uploads overlap the previous
+        # step's read-back)
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         ho = torch.empty_like(hq).pin_memory()
 
         def e2e_step():
-            b2.flash_attn_fwd_host(hq, hk, hv, causal=True, out=ho)
+            b2.flash_attn_fwd_host(hq, hk, hv, causal=True, out=ho, host_inputs_ready=True)
 
         for _ in range(args.warmup):
             e2e_step()

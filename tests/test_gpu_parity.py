@@ -559,7 +559,7 @@ def test_gemm_softmax_epilogue_fp32_and_limits():
 
 
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("chunks", [1, 3, 64])
+@pytest.mark.parametrize("chunks", [None, 1, 3, 64])
 def test_fa_host_pipeline_matches_device_path(causal, chunks):
     """flash_attn_fwd_host (host tensors, copies overlapped with the kernel per
     (batch, head) chunk) returns exactly what the device entry point returns."""
@@ -572,16 +572,20 @@ def test_fa_host_pipeline_matches_device_path(causal, chunks):
     _check(o, O.ref_attention(q, k, v, causal), torch.float16)
 
 
-def test_fa_host_pipeline_back_to_back_calls_reuse_staging():
+@pytest.mark.parametrize("ready", [False, True])
+def test_fa_host_pipeline_back_to_back_calls_reuse_staging(ready):
     """Calls queued without synchronising, with inputs that grow and shrink: the
     two device staging slots are reused (and regrown) only after the call that
-    last used them has read its output back, so every output is intact."""
+    last used them has read its output back, so every output is intact; with
+    host_inputs_ready the uploads of one call overlap the previous read-back."""
     shapes = [(1, 4, 256, 64), (2, 6, 300, 64), (1, 3, 128, 128), (2, 8, 512, 64), (1, 2, 64, 32),
               (2, 8, 512, 64), (1, 4, 256, 64)]
     cases = []
     for i, shp in enumerate(shapes):
         q, k, v = (_rand(shp, torch.float16, 200 + 3 * i + s, 0.5).pin_memory() for s in range(3))
-        cases.append((q, k, v, b2.flash_attn_fwd_host(q, k, v, causal=bool(i & 1), chunks=3)))
+        cases.append((q, k, v, b2.flash_attn_fwd_host(q, k, v, causal=bool(i & 1),
+                                                      chunks=3 if i % 3 else None,
+                                                      host_inputs_ready=ready)))
     torch.cuda.synchronize()
     for i, (q, k, v, o) in enumerate(cases):
         ref = b2.flash_attn_fwd(q.to(DEV), k.to(DEV), v.to(DEV), causal=bool(i & 1)).cpu()

@@ -120,3 +120,19 @@ def test_surviving_rank_gets_an_error_not_a_hang():
 
 
 _free_port_shared = [_free_port()]
+
+
+def test_host_pipeline_chunk_bounds():
+    from triton_msl_b200.host_pipeline import _chunk_bounds
+    # default: 10/16, 5/16, 1/16 of the (batch, head) slices, largest first
+    assert _chunk_bounds(64, None) == [0, 40, 60, 64]
+    assert _chunk_bounds(2048, None) == [0, 1280, 1920, 2048]
+    # uploads overlapping the previous read-back: 2/3 and 1/3
+    assert _chunk_bounds(64, None, True) == [0, 43, 64]
+    for bh in range(1, 70):
+        for chunks, ready in [(c, r) for c in (None, 1, 2, 3, 4, 64, 1000) for r in (False, True)]:
+            b = _chunk_bounds(bh, chunks, ready)
+            assert b[0] == 0 and b[-1] == bh
+            assert all(x < y for x, y in zip(b, b[1:])), (bh, chunks, b)
+            if chunks is not None:
+                assert len(b) - 1 == min(chunks, bh)
