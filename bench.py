@@ -267,6 +267,35 @@ def cpu_gemm(cfg, seconds, threads, model, rows=None):
                         extrapolated=sub is not cfg)
 
 
+def cpu_gemm_chain(cfg, chain, seconds, threads, model, rows=256):
+    """Oracle GEMM + epilogue chain on the first `rows` rows of A, extrapolated per FLOP."""
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    import dataclasses
+    sub = dataclasses.replace(cfg, M=min(rows, cfg.M))
+    a, bm, bias = W.gemm_inputs(sub, seed=1)
+    rate, n, dt = cpu_rate(lambda: O.ref_gemm_epilogue(a, bm, chain, bias, torch.float16),
+                           sub.flops(), seconds)
+    sample = (f"{n} x A[{sub.M},{sub.K}] @ B[{sub.K},{sub.N}] with the chain "
+              f"{[c[0] for c in chain]}, fp32 torch-CPU oracle, {dt:.1f}s")
+    return cpu_baseline(round(rate / 1e12, 5), "TFLOP/s", sample, threads, model,
+                        extrapolated=sub.M != cfg.M)
+
+
+def cpu_reduce_axis(cfg, seconds, threads, model, rows=4096):
+    """Oracle sum over dim 0 of the first `rows` rows of X, per byte read."""
+    from oracle import oracle as O
+    from triton_msl_b200 import workloads as W
+    import dataclasses
+    sub = dataclasses.replace(cfg, rows=min(rows, cfg.rows))
+    x, _, _ = W.row_inputs(sub, seed=1)
+    byt = sub.rows * sub.cols * 4 + sub.cols * 4
+    rate, n, dt = cpu_rate(lambda: O.ref_reduce_axis(x, "sum", 0), byt, seconds)
+    sample = f"{n} x sum over dim 0 of X[{sub.rows},{sub.cols}] fp32, torch-CPU oracle, {dt:.1f}s"
+    return cpu_baseline(round(rate / 1e9, 3), "GB/s", sample, threads, model,
+                        extrapolated=sub.rows != cfg.rows)
+
+
 def cpu_rows(cfg, op, seconds, threads, model, rows=4096):
     from oracle import oracle as O
     from triton_msl_b200 import workloads as W
@@ -640,6 +669,8 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
         "per_rank_ms": [round(x_, 4) for x_ in per], "kernel": kname,
         "roofline": roofline(kname, gbs, float(peaks["hbm_gbs"]), "GB/s", "hbm",
                              traffic.get(f"{r.name}_sum_dim0"), peak_kind + " copy")}
+    if do_cpu:
+        out[f"{r.name}_sum_dim0"]["cpu_baseline"] = cpu_reduce_axis(r, cs, threads, model)
     del x, w, bb
     # GEMM 8192^3 fp16 with a general epilogue chain (bias, scale, GELU, clamp)
     a, bm, bias = W.gemm_inputs(g, device=dev, seed=rank)
@@ -655,6 +686,8 @@ def run_extras(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu,
         "roofline": roofline(kname, ach, float(peaks["bf16_tflops"]), "TFLOP/s", "tensor",
                              traffic.get("gemm_f16_8192_epilogue_chain"),
                              peak_kind + " bf16 burst")}
+    if do_cpu:
+        out["gemm_f16_8192_epilogue_chain"]["cpu_baseline"] = cpu_gemm_chain(g, chain, cs, threads, model)
     del a, bm, bias
     return out
 

@@ -496,7 +496,7 @@ fa_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int i = 4; i < kBN; i += 8) {
         mq[0] = fmax3(mq[0], s[i], s[i + 1]);
         mq[1] = fmax3(mq[1], s[i + 2], s[i + 3]);
-        mq[2] = fmax3(mq[2], s[i + 4], i + 5 < kBN ? s[i + 5] : -INFINITY);
+        mq[2] = fmax3(mq[2], i + 4 < kBN ? s[i + 4] : -INFINITY, i + 5 < kBN ? s[i + 5] : -INFINITY);
         mq[3] = fmax3(mq[3], i + 6 < kBN ? s[i + 6] : -INFINITY, i + 7 < kBN ? s[i + 7] : -INFINITY);
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale_log2;
