@@ -655,7 +655,7 @@ constexpr int kAxisUnroll = 8, kAxisWant = 4;
 // addresses: every warp load is coalesced) and walks its R range; grid.z splits R
 // when the (inner, outer) grid alone would not fill the SMs, partials to the
 // workspace and a second pass folds them in split order.
-template <typename T, int OP, int VEC>
+template <typename T, int OP, int VEC, typename IDX>
 __global__ void __launch_bounds__(256)
 axis_reduce_kernel(const T* __restrict__ x, long long outer, long long R, long long inner,
                    long long r_chunk, int splits, Partial* __restrict__ ws, void* __restrict__ out) {
@@ -663,41 +663,58 @@ axis_reduce_kernel(const T* __restrict__ x, long long outer, long long R, long l
   if (i0 >= inner) return;
   const long long r0 = (long long)blockIdx.z * r_chunk;
   const long long r1 = r0 + r_chunk < R ? r0 + r_chunk : R;
+  if (r0 >= r1) return;
   constexpr bool ARG = OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN;
   constexpr bool MAXI = OP == B2_ROW_ARGMAX;
-  for (long long o = blockIdx.y; o < outer; o += gridDim.y) {
-    float acc[VEC];
-    long long idx[VEC];
+  // one row's VEC elements of this thread as fp32
+  auto load = [&](const T* xo, long long r, float (&f)[VEC]) {
+    if constexpr (VEC == 4 && sizeof(T) == 4) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(xo + r * inner));
+      f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
+    } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      acc[e] = (OP == B2_ROW_SUM) ? 0.f
-             : (OP == B2_ROW_MAX || OP == B2_ROW_ARGMAX) ? -INFINITY : INFINITY;
-      idx[e] = 0x7fffffffffffffffLL;
+      for (int e = 0; e < VEC; ++e) f[e] = (i0 + e < inner) ? to_f32<T>(xo[r * inner + e]) : 0.f;
     }
+  };
+  // Fold one later row into the running value. Rows arrive in ascending order,
+  // so for argmax/argmin a tie keeps the earlier row (the lower index) and the
+  // first NaN, once taken, is never replaced. IDX is the row offset from r0.
+  auto fold = [&](float& a, IDX& ia, float f, IDX rf) {
+    if constexpr (ARG) {
+      const bool better = (MAXI ? f > a : f < a) || (f != f && a == a);
+      a = better ? f : a;
+      ia = better ? rf : ia;
+    } else if constexpr (OP == B2_ROW_SUM) {
+      a += f;
+    } else if constexpr (OP == B2_ROW_MAX) {
+      a = nan_max(a, f);
+    } else {
+      a = nan_min(a, f);
+    }
+  };
+  for (long long o = blockIdx.y; o < outer; o += gridDim.y) {
     const T* xo = x + o * R * inner + i0;
-    // unrolled so several rows' loads are in flight per thread
-#pragma unroll kAxisUnroll
-    for (long long r = r0; r < r1; ++r) {
+    float acc[VEC];
+    IDX idx[VEC];
+    load(xo, r0, acc);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) idx[e] = 0;
+    long long r = r0 + 1;
+    // kAxisUnroll rows' loads issued before any of them is folded
+    for (; r + kAxisUnroll <= r1; r += kAxisUnroll) {
+      float f[kAxisUnroll][VEC];
+#pragma unroll
+      for (int u = 0; u < kAxisUnroll; ++u) load(xo, r + u, f[u]);
+#pragma unroll
+      for (int u = 0; u < kAxisUnroll; ++u)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) fold(acc[e], idx[e], f[u][e], (IDX)(r + u - r0));
+    }
+    for (; r < r1; ++r) {
       float f[VEC];
-      if constexpr (VEC == 4 && sizeof(T) == 4) {
-        const float4 q = __ldcs(reinterpret_cast<const float4*>(xo + r * inner));
-        f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
-      } else {
+      load(xo, r, f);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) f[e] = (i0 + e < inner) ? to_f32<T>(xo[r * inner + e]) : 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        if (ARG) {
-          if (arg_better<MAXI>(f[e], r, acc[e], idx[e])) { acc[e] = f[e]; idx[e] = r; }
-        } else if (OP == B2_ROW_SUM) {
-          acc[e] += f[e];
-        } else if (OP == B2_ROW_MAX) {
-          acc[e] = nan_max(acc[e], f[e]);
-        } else {
-          acc[e] = nan_min(acc[e], f[e]);
-        }
-      }
+      for (int e = 0; e < VEC; ++e) fold(acc[e], idx[e], f[e], (IDX)(r - r0));
     }
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
@@ -707,10 +724,10 @@ axis_reduce_kernel(const T* __restrict__ x, long long outer, long long R, long l
         Partial p;
         p.v = acc[e];
         p.pad = 0;
-        p.i = idx[e];
+        p.i = r0 + (long long)idx[e];
         ws[(long long)blockIdx.z * outer * inner + oi] = p;
       } else if (ARG) {
-        reinterpret_cast<long long*>(out)[oi] = idx[e];
+        reinterpret_cast<long long*>(out)[oi] = r0 + (long long)idx[e];
       } else {
         reinterpret_cast<T*>(out)[oi] = from_f32<T>(acc[e]);
       }
@@ -728,6 +745,7 @@ axis_reduce_final_kernel(const Partial* __restrict__ ws, long long n, int splits
     Partial p = ws[k];
     float a = p.v;
     long long ai = p.i;
+#pragma unroll 8
     for (int sp = 1; sp < splits; ++sp) {
       const Partial q = ws[(long long)sp * n + k];
       if (ARG) {
@@ -783,12 +801,20 @@ int axis_launch(const void* x, void* out, long long outer, long long R, long lon
     p.r_chunk = R;
   }
   const dim3 grid((unsigned)p.xblocks, (unsigned)(outer < 65535 ? outer : 65535), (unsigned)p.splits);
-  if (p.vec == 4)
-    axis_reduce_kernel<T, OP, 4><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk, p.splits,
-                                                       (Partial*)ws, out);
+  // row offsets within a split as int32 unless a split spans 2^31 rows
+  const bool wide = p.r_chunk > 0x7fffffffLL;
+  if (p.vec == 4 && !wide)
+    axis_reduce_kernel<T, OP, 4, int><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk,
+                                                            p.splits, (Partial*)ws, out);
+  else if (p.vec == 4)
+    axis_reduce_kernel<T, OP, 4, long long><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk,
+                                                                  p.splits, (Partial*)ws, out);
+  else if (!wide)
+    axis_reduce_kernel<T, OP, 1, int><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk,
+                                                            p.splits, (Partial*)ws, out);
   else
-    axis_reduce_kernel<T, OP, 1><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk, p.splits,
-                                                       (Partial*)ws, out);
+    axis_reduce_kernel<T, OP, 1, long long><<<grid, 256, 0, st>>>((const T*)x, outer, R, inner, p.r_chunk,
+                                                                  p.splits, (Partial*)ws, out);
   B2_CHECK_LAUNCH();
   if (p.splits > 1) {
     const long long n = outer * inner;
