@@ -437,6 +437,51 @@ def test_row_split_path_long_rows(op):
         assert torch.equal(got.cpu(), ref)
 
 
+@pytest.mark.parametrize("op", ROW_OPS)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_row_long_rows_match_oracle(op, dtype):
+    """Rows past the register-resident limit (two-pass long-row kernel): row 1
+    rises steadily, so the online softmax max grows in every vector and the
+    running sum is rescaled throughout; row 2 has a tie for the maximum."""
+    rows, cols = 6, 65536 + 24
+    x = _rand((rows, cols), torch.float32, 91)
+    x[1] = torch.linspace(-20.0, 20.0, cols)
+    x[2, 100] = x[2, 60000] = 50.0
+    x = x.to(dtype)
+    w = (1 + 0.1 * _rand((cols,), torch.float32, 3)).to(dtype)
+    b = (0.1 * _rand((cols,), torch.float32, 4)).to(dtype)
+    got = _row_run(op, x.to(DEV), w.to(DEV), b.to(DEV))
+    ref = _row_ref(op, x, w, b)
+    if op.startswith("arg"):
+        assert torch.equal(got.cpu(), ref)
+    elif op == "sum":
+        # 65K-element sums of values up to +-20: against a float64 sum, relative to sum|x|
+        exact = x.double().sum(-1)
+        err = (got.cpu().double() - exact).abs() / x.double().abs().sum(-1)
+        assert err.max() < (1e-6 if dtype == torch.float32 else 4e-3)
+    else:
+        _check(got, ref, dtype)
+
+
+def test_row_long_rows_nan_tie_inf():
+    x = torch.randn(6, 70000)
+    x[0, :] = 2.0                       # all equal: index 0
+    x[1, 10] = x[1, 69000] = 99.0       # tie: lower index
+    x[2, 50000] = float("nan")          # NaN wins argmax / argmin / max / min
+    x[3, 7] = x[3, 65000] = float("nan")
+    x[4, :] = float("-inf")
+    x[5, :] = float("inf")
+    xd = x.to(DEV)
+    assert torch.equal(b2.row_argmax(xd).cpu(), O.ref_argmax(x))
+    assert torch.equal(b2.row_argmin(xd).cpu(), O.ref_argmin(x))
+    assert torch.allclose(b2.row_max(xd).cpu(), O.ref_max(x), equal_nan=True)
+    assert torch.allclose(b2.row_min(xd).cpu(), O.ref_min(x), equal_nan=True)
+    sm = b2.row_softmax(xd).cpu()
+    assert torch.isnan(sm[2]).all() and torch.isnan(sm[4]).all()
+    assert torch.allclose(sm[0], torch.full((70000,), 1 / 70000.0), rtol=1e-5)
+    assert torch.allclose(sm[1], O.ref_softmax(x[1:2])[0], atol=1e-6)
+
+
 def test_row_nan_and_tie_semantics():
     x = torch.randn(8, 300)
     x[0, :] = 2.0

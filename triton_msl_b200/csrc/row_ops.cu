@@ -436,6 +436,226 @@ row_generic_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __
   }
 }
 
+// ------------------------------------------------------------ long rows
+// Rows too long for the register-resident kernel (cols > 32K, 16-byte aligned):
+// one 512-thread CTA per row, two CTAs per SM, 16-byte loads with four in
+// flight per thread. Pass 1 reads the row once and keeps per-thread running
+// statistics (online max and sum of exponentials for softmax, sums shifted by
+// the thread's first element for LayerNorm, the sum of squares for RMSNorm;
+// sum / max / min / argmax / argmin finish here). Pass 2 re-reads the row,
+// which the ~300 rows in flight leave in L2 for rows up to ~100K fp32
+// columns, and writes the output.
+// Measured on B200 (4096 x 65536 and 512 x 524288 fp32): two CTAs per SM with
+// four 16-byte loads in flight per thread beat one CTA per SM with four or
+// eight by 5-30 %.
+constexpr int kLongTPR = 512, kLongU = 4, kLongCtas = 2;
+
+// (m, s): running max m (NaN-propagating) and sum s of 2^((x - m) * log2 e)
+__device__ __forceinline__ void sm_combine(float& m, float& s, float m2, float s2) {
+  const float mm = nan_max(m, m2);
+  const float a = (m == mm) ? s : s * exp2f((m - mm) * kLog2e);
+  const float b = (m2 == mm) ? s2 : s2 * exp2f((m2 - mm) * kLog2e);
+  m = mm;
+  s = a + b;
+}
+// (n, mean, M2) of two disjoint sets (Chan et al.'s pairwise update)
+__device__ __forceinline__ void mv_combine(float& n, float& mean, float& m2, float nb, float meanb,
+                                           float m2b) {
+  if (nb == 0.f) return;
+  if (n == 0.f) { n = nb; mean = meanb; m2 = m2b; return; }
+  const float nt = n + nb, d = meanb - mean;
+  mean = fmaf(d, nb / nt, mean);
+  m2 = m2 + m2b + d * d * (n * nb / nt);
+  n = nt;
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(kLongTPR, kLongCtas)
+row_long_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bvec,
+                void* __restrict__ out, long long rows, int cols, long long ldx, long long ldo,
+                float eps) {
+  constexpr int EPV = Vec<T>::N, TPR = kLongTPR, NW = TPR / 32;
+  constexpr int U = sizeof(T) == 4 ? kLongU : kLongU / 2;  // 16-bit types: 8 values per vector
+  __shared__ float red_a[NW], red_b[NW], red_c[NW];
+  __shared__ int red_i[NW];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nvec = cols / EPV;
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* xr = x + row * ldx;
+    // pass 1
+    float a0, a1 = 0.f, a2 = 0.f;  // per-op running statistics
+    int ai = 0x7fffffff;
+    float shift = 0.f;
+    if constexpr (OP == B2_ROW_SUM || OP == B2_ROW_RMSNORM) a0 = 0.f;
+    else if constexpr (OP == B2_ROW_MAX || OP == B2_ROW_ARGMAX || OP == B2_ROW_SOFTMAX) a0 = -INFINITY;
+    else if constexpr (OP == B2_ROW_MIN || OP == B2_ROW_ARGMIN) a0 = INFINITY;
+    else a0 = 0.f;  // LayerNorm: a0 = count, a1 = sum of (x - shift), a2 = sum of squares
+    if constexpr (OP == B2_ROW_LAYERNORM) {
+      if (tid < nvec) shift = to_f32<T>(xr[tid * EPV]);
+    }
+    for (int k0 = tid; k0 < nvec; k0 += TPR * U) {
+      float v[U][EPV];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (k0 + u * TPR < nvec) {
+          const uint4 q = *reinterpret_cast<const uint4*>(xr + (long long)(k0 + u * TPR) * EPV);
+          if constexpr (sizeof(T) == 4) {
+            v[u][0] = __uint_as_float(q.x); v[u][1] = __uint_as_float(q.y);
+            v[u][2] = __uint_as_float(q.z); v[u][3] = __uint_as_float(q.w);
+          } else {
+            const T* h = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) v[u][j] = to_f32<T>(h[j]);
+          }
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (k0 + u * TPR >= nvec) break;
+        if constexpr (OP == B2_ROW_SUM) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) a0 += v[u][j];
+        } else if constexpr (OP == B2_ROW_MAX) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) a0 = nan_max(a0, v[u][j]);
+        } else if constexpr (OP == B2_ROW_MIN) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) a0 = nan_min(a0, v[u][j]);
+        } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+          // elements arrive in ascending column order: a tie keeps the earlier
+          // column, the first NaN is kept
+          const int c = (k0 + u * TPR) * EPV;
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            const float f = v[u][j];
+            const bool better = (OP == B2_ROW_ARGMAX ? f > a0 : f < a0) || (f != f && a0 == a0) ||
+                                ai == 0x7fffffff;
+            a0 = better ? f : a0;
+            ai = better ? c + j : ai;
+          }
+        } else if constexpr (OP == B2_ROW_SOFTMAX) {
+          float mv = a0;
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) mv = nan_max(mv, v[u][j]);
+          if (mv != a0) {  // the max grew (or turned NaN): rescale the sum
+            a1 = (a0 == -INFINITY) ? 0.f : a1 * exp2f((a0 - mv) * kLog2e);
+            a0 = mv;
+          }
+          const float ms = a0 == -INFINITY ? 0.f : a0 * kLog2e;
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) a1 += exp2f(fmaf(v[u][j], kLog2e, -ms));
+        } else if constexpr (OP == B2_ROW_LAYERNORM) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            const float d = v[u][j] - shift;
+            a1 += d;
+            a2 = fmaf(d, d, a2);
+          }
+          a0 += (float)EPV;
+        } else {  // RMSNorm
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) a0 = fmaf(v[u][j], v[u][j], a0);
+        }
+      }
+    }
+    // combine across the CTA: warp shuffles, then one value per warp in shared
+    // memory, folded in warp order by every thread
+    if constexpr (OP == B2_ROW_LAYERNORM) {
+      // (count, sum of x - shift, sum of squares) -> (count, mean, M2)
+      float n = a0, mean = a0 > 0.f ? shift + a1 / a0 : 0.f;
+      float m2 = a0 > 0.f ? fmaxf(a2 - a1 * a1 / a0, 0.f) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float nb = __shfl_xor_sync(0xffffffffu, n, o), mb = __shfl_xor_sync(0xffffffffu, mean, o),
+                    qb = __shfl_xor_sync(0xffffffffu, m2, o);
+        mv_combine(n, mean, m2, nb, mb, qb);
+      }
+      __syncthreads();
+      if (lane == 0) { red_a[wid] = n; red_b[wid] = mean; red_c[wid] = m2; }
+      __syncthreads();
+      n = red_a[0]; mean = red_b[0]; m2 = red_c[0];
+      for (int i = 1; i < NW; ++i) mv_combine(n, mean, m2, red_a[i], red_b[i], red_c[i]);
+      a1 = mean;
+      a2 = rsqrtf(m2 / (float)cols + eps);
+    } else if constexpr (OP == B2_ROW_SOFTMAX) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float mb = __shfl_xor_sync(0xffffffffu, a0, o), sb = __shfl_xor_sync(0xffffffffu, a1, o);
+        sm_combine(a0, a1, mb, sb);
+      }
+      __syncthreads();
+      if (lane == 0) { red_a[wid] = a0; red_b[wid] = a1; }
+      __syncthreads();
+      a0 = red_a[0]; a1 = red_b[0];
+      for (int i = 1; i < NW; ++i) sm_combine(a0, a1, red_a[i], red_b[i]);
+    } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+      constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+      __syncthreads();
+      row_reduce_arg<TPR, MAXI>(a0, ai, red_a, red_i);
+      if (tid == 0) reinterpret_cast<long long*>(out)[row] = (long long)ai;
+      continue;
+    } else {
+      constexpr int KIND = (OP == B2_ROW_SUM || OP == B2_ROW_RMSNORM) ? RK_SUM
+                         : (OP == B2_ROW_MAX ? RK_MAX : RK_MIN);
+      a0 = row_reduce<TPR, KIND>(a0, red_a);
+      if constexpr (OP == B2_ROW_SUM || OP == B2_ROW_MAX || OP == B2_ROW_MIN) {
+        if (tid == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a0);
+        continue;
+      }
+    }
+    // pass 2: normalise and write
+    T* o = reinterpret_cast<T*>(out) + row * ldo;
+    float ms = 0.f, inv = 0.f;
+    if constexpr (OP == B2_ROW_SOFTMAX) {
+      ms = a0 == -INFINITY ? 0.f : a0 * kLog2e;
+      inv = 1.f / a1;
+    } else if constexpr (OP == B2_ROW_RMSNORM) {
+      inv = rsqrtf(a0 / (float)cols + eps);
+    }
+    // last chunk first: the most recently read part of the row is the most
+    // likely to be still in L2
+    for (int kb = ((nvec - 1) / (TPR * U)) * (TPR * U); kb >= 0; kb -= TPR * U) {
+      const int k0 = kb + tid;
+      float v[U][EPV];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (k0 + u * TPR < nvec) ld_vec<T>(xr + (long long)(k0 + u * TPR) * EPV, v[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = k0 + u * TPR;
+        if (k >= nvec) break;
+        if constexpr (OP == B2_ROW_SOFTMAX) {
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[u][j] = exp2f(fmaf(v[u][j], kLog2e, -ms)) * inv;
+        } else if constexpr (OP == B2_ROW_LAYERNORM) {
+          float g[EPV], bb[EPV];
+          if (w) ld_vec_cached<T>(w + (long long)k * EPV, g);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) g[j] = 1.f;
+          }
+          if (bvec) ld_vec_cached<T>(bvec + (long long)k * EPV, bb);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) bb[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[u][j] = fmaf((v[u][j] - a1) * a2, g[j], bb[j]);
+        } else {
+          float g[EPV];
+          if (w) ld_vec_cached<T>(w + (long long)k * EPV, g);
+          else {
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) g[j] = 1.f;
+          }
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) v[u][j] = v[u][j] * inv * g[j];
+        }
+        st_vec<T>(o + (long long)k * EPV, v[u]);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------- split-row reduction
 // Few long rows: grid (splits, rows). Each CTA reduces one chunk into the
 // workspace; a second launch folds the partials in chunk order.
@@ -610,6 +830,15 @@ int dispatch_op(const void* x, const void* w, const void* b, void* out, long lon
                        (!row_out || (ldo % EPV == 0 && al16(out)));
   if (aligned && cols <= 32 * 1024 && cols > 0) {
     return dispatch_reg<T, OP>(x, w, b, out, rows, (int)cols, ldx, ldo, eps, st);
+  }
+  if (aligned && cols < (1LL << 31)) {
+    long long blocks = rows;
+    const long long cap = (long long)num_sms() * kLongCtas;
+    if (blocks > cap) blocks = cap;
+    row_long_kernel<T, OP><<<(unsigned)blocks, kLongTPR, 0, st>>>((const T*)x, (const T*)w, (const T*)b,
+                                                                 out, rows, (int)cols, ldx, ldo, eps);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
   }
   long long blocks = rows;
   const long long cap = (long long)num_sms() * 16;
