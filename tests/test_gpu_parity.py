@@ -482,6 +482,26 @@ def test_row_long_rows_nan_tie_inf():
     assert torch.allclose(sm[1], O.ref_softmax(x[1:2])[0], atol=1e-6)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("cols", [8, 1000, 4096, 32768])
+def test_row_arg_16bit_ties_nan(dtype, cols):
+    """argmax / argmin over fp16 / bf16 rows (values compared two at a time in
+    their own type): small integers make ties everywhere (lowest column wins),
+    plus NaN (first NaN wins), all -inf and all-equal rows."""
+    g = torch.Generator().manual_seed(cols)
+    x = torch.randint(-3, 4, (40, cols), generator=g).to(dtype)
+    x[1, cols // 2] = float("nan")
+    x[2, cols - 1] = float("nan")
+    x[2, cols // 3] = float("nan")
+    x[3, :] = float("-inf")
+    x[4, :] = float("inf")
+    x[5, :] = 1.0
+    x[6, cols - 1] = 100.0
+    xd = x.to(DEV)
+    assert torch.equal(b2.row_argmax(xd).cpu(), O.ref_argmax(x))
+    assert torch.equal(b2.row_argmin(xd).cpu(), O.ref_argmin(x))
+
+
 def test_row_nan_and_tie_semantics():
     x = torch.randn(8, 300)
     x[0, :] = 2.0

@@ -191,13 +191,19 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
     const long long row = row0 + rloc;
     const bool row_ok = row < rows;
     const T* xr = x + (row_ok ? row : 0) * ldx;
+    // argmax / argmin over 16-bit inputs compare the raw pairs (see below)
+    constexpr bool PACKED_ARG = (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) && sizeof(T) == 2;
     float v[VPT][EPV];
+    uint4 raw[PACKED_ARG ? VPT : 1];
     bool ok[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = (sub + i * TPR) * EPV;
       ok[i] = row_ok && c < cols;
-      if (ok[i]) ld_vec<T>(xr + c, v[i]);
+      if (ok[i]) {
+        if constexpr (PACKED_ARG) raw[i] = __ldcs(reinterpret_cast<const uint4*>(xr + c));
+        else ld_vec<T>(xr + c, v[i]);
+      }
     }
 
     if constexpr (OP == B2_ROW_SUM || OP == B2_ROW_MAX || OP == B2_ROW_MIN) {
@@ -214,6 +220,55 @@ row_reg_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __rest
         }
       a = row_reduce<TPR, OP == B2_ROW_SUM ? RK_SUM : (OP == B2_ROW_MAX ? RK_MAX : RK_MIN)>(a, red_v);
       if (row_ok && sub == 0) reinterpret_cast<T*>(out)[row] = from_f32<T>(a);
+    } else if constexpr (PACKED_ARG) {
+      // 16-bit inputs: four chains of value pairs per thread, compared two at a
+      // time in the inputs' own type (exact: no conversion is needed to order
+      // them) with bitwise selects of the values and of 16-bit column indices
+      // (register-path rows have < 2^15 columns). The per-pair rule is the
+      // scalar chains' rule below: take x when !(x <= best) and best is not
+      // NaN, so ties keep the earlier column and the first NaN wins.
+      constexpr bool MAXI = OP == B2_ROW_ARGMAX;
+      using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+      auto as2 = [](uint32_t u) { T2 r; memcpy(&r, &u, 4); return r; };
+      const uint32_t inf2 = std::is_same<T, __half>::value ? (MAXI ? 0xFC00FC00u : 0x7C007C00u)
+                                                           : (MAXI ? 0xFF80FF80u : 0x7F807F80u);
+      uint32_t cv[EPV / 2], ck[EPV / 2];
+#pragma unroll
+      for (int p = 0; p < EPV / 2; ++p) {
+        const uint32_t c0 = (uint32_t)(sub * EPV + 2 * p);
+        cv[p] = ok[0] ? (&raw[0].x)[p] : inf2;
+        ck[p] = ok[0] ? (c0 | ((c0 + 1) << 16)) : 0xFFFFFFFFu;
+      }
+#pragma unroll
+      for (int i = 1; i < VPT; ++i)
+        if (ok[i]) {
+#pragma unroll
+          for (int p = 0; p < EPV / 2; ++p) {
+            const uint32_t xv = (&raw[i].x)[p];
+            const uint32_t notbetter = MAXI ? __hle2_mask(as2(xv), as2(cv[p])) : __hge2_mask(as2(xv), as2(cv[p]));
+            const uint32_t take = ~notbetter & __heq2_mask(as2(cv[p]), as2(cv[p]));
+            const uint32_t c0 = (uint32_t)((sub + i * TPR) * EPV + 2 * p);
+            cv[p] = (cv[p] & ~take) | (xv & take);
+            ck[p] = (ck[p] & ~take) | ((c0 | ((c0 + 1) << 16)) & take);
+          }
+        }
+      float bv = MAXI ? -INFINITY : INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int p = 0; p < EPV / 2; ++p) {
+#pragma unroll
+        for (int hsel = 0; hsel < 2; ++hsel) {
+          const uint16_t hb = (uint16_t)(hsel ? cv[p] >> 16 : cv[p] & 0xFFFFu);
+          T hv;
+          memcpy(&hv, &hb, 2);
+          const uint32_t ix = hsel ? ck[p] >> 16 : ck[p] & 0xFFFFu;
+          const int ii = ix == 0xFFFFu ? 0x7fffffff : (int)ix;
+          const float fv = to_f32<T>(hv);
+          if (arg_better<MAXI>(fv, ii, bv, bi)) { bv = fv; bi = ii; }
+        }
+      }
+      row_reduce_arg<TPR, MAXI>(bv, bi, red_av[parity], red_ai[parity]);
+      if (row_ok && sub == 0) reinterpret_cast<long long*>(out)[row] = (long long)bi;
     } else if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
       constexpr bool MAXI = OP == B2_ROW_ARGMAX;
       // One independent scan per vector lane j (EPV chains, so the compare /
@@ -768,6 +823,20 @@ int dispatch_reg(const void* x, const void* w, const void* b, void* out, long lo
   constexpr int EPV = Vec<T>::N;
   constexpr int V16 = 16 / EPV;  // vectors per thread for 16 elements
   const int per16 = (cols + 15) / 16;
+  if constexpr ((OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) && sizeof(T) == 2) {
+    // packed 16-bit compares make each element cheap, so the per-row
+    // cross-thread reduction dominates: 64 elements per thread (B200, fp16 /
+    // bf16 argmax: 768 columns 1666 -> 3448 GB/s, 1024 2351 -> 4948, 4096
+    // 3604 -> 4110 against 16-32 elements per thread)
+    const int per64 = (cols + 63) / 64;
+    if (per64 <= 8) return launch_reg<T, OP, 8, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    if (per64 <= 16) return launch_reg<T, OP, 16, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    if (per64 <= 32) return launch_reg<T, OP, 32, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    if (per64 <= 64) return launch_reg<T, OP, 64, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    if (per64 <= 128) return launch_reg<T, OP, 128, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    if (per64 <= 256) return launch_reg<T, OP, 256, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    return launch_reg<T, OP, 512, 4 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+  }
   if constexpr (OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
     // index tracking doubles the cross-thread reduction: 32 elements per
     // thread halve the threads per row (65536x4096 fp32 on B200: 0.86 -> 0.96
