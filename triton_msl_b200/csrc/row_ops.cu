@@ -850,6 +850,27 @@ int dispatch_reg(const void* x, const void* w, const void* b, void* out, long lo
       return launch_reg<T, OP, 1024, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
     }
   }
+  if constexpr (OP == B2_ROW_SOFTMAX || OP == B2_ROW_LAYERNORM || OP == B2_ROW_RMSNORM ||
+                OP == B2_ROW_ARGMAX || OP == B2_ROW_ARGMIN) {
+    // 32 elements per thread above 512 columns: half the threads per row, so
+    // a row of <= 1024 elements is one warp (no shared-memory hop) and long
+    // rows need fewer barriers per reduction. Measured on B200 against 16 per
+    // thread: fp32 softmax 1024 columns 4946 -> 6402 GB/s, 16384 columns
+    // 4262 -> 6473; fp16 softmax 768 columns 4011 -> 5008; bf16 LayerNorm 8192
+    // columns 3987 -> 4569; 256 columns lose (LayerNorm 6251 -> 5606), and
+    // fp32 rows of 4096 lose 1-3 % (softmax 6449 -> 6392, LayerNorm 6416 ->
+    // 6251), so short rows and fp32 rows of 1K-8K columns keep 16.
+    const bool e32 = cols > 512 && (sizeof(T) == 2 || cols <= 1024 || cols > 8192);
+    if (e32) {
+      const int per32 = (cols + 31) / 32;
+      if (per32 <= 32) return launch_reg<T, OP, 32, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 64) return launch_reg<T, OP, 64, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 128) return launch_reg<T, OP, 128, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 256) return launch_reg<T, OP, 256, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      if (per32 <= 512) return launch_reg<T, OP, 512, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+      return launch_reg<T, OP, 1024, 2 * V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
+    }
+  }
   if (per16 <= 8) return launch_reg<T, OP, 8, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
   if (per16 <= 16) return launch_reg<T, OP, 16, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
   if (per16 <= 32) return launch_reg<T, OP, 32, V16>(x, w, b, out, rows, cols, ldx, ldo, eps, st);
