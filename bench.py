@@ -858,7 +858,8 @@ def run_scale(args, world, rank, dev, flush, peaks, peak_kind, traffic, do_cpu, 
 
 ONLY = ("headline", "fa_d64", "fa_d32", "fa_bf16", "fa_f32", "gemm_f16", "gemm_f32",
         "rows_softmax", "rows_layernorm", "rows_rmsnorm", "rows_sum", "rows_max", "rows_argmax",
-        "gemm_bf16_scale_shard", "rows_sum_dim0", "gemm_f16_chain")
+        "gemm_bf16_scale_shard", "rows_sum_dim0", "gemm_f16_chain", "rows_argmax_dim0",
+        "rows_long_softmax", "rows_long_argmax", "rows_f16_argmax")
 
 
 def run_only(args):
@@ -892,6 +893,23 @@ def run_only(args):
         x, _, _ = W.row_inputs(r, device=dev)
         fn = lambda: b2.reduce(x, "sum", 0)
         work, unit = r.rows * r.cols * 4 + r.cols * 4, "GB/s"
+    elif name == "rows_argmax_dim0":
+        r = W.ROWS_F32
+        x, _, _ = W.row_inputs(r, device=dev)
+        fn = lambda: b2.reduce(x, "argmax", 0)
+        work, unit = r.rows * r.cols * 4 + r.cols * 8, "GB/s"
+    elif name in ("rows_long_softmax", "rows_long_argmax", "rows_f16_argmax"):
+        # rows past the register-resident limit (fp32 [4096, 65536]) and 16-bit
+        # argmax (fp16 [65536, 4096]): same seeded N(0, 1) values
+        shape, dt = ((4096, 65536), torch.float32) if "long" in name else ((65536, 4096), torch.float16)
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(*shape, device=dev, generator=g).to(dt)
+        rd = x.numel() * x.element_size()
+        if name == "rows_long_softmax":
+            fn, work = (lambda: b2.row_softmax(x)), 2 * rd
+        else:
+            fn, work = (lambda: b2.row_argmax(x)), rd + 8 * shape[0]
+        unit = "GB/s"
     elif name == "gemm_bf16_scale_shard":
         cfg = W.GEMM_BF16_SCALE
         a = torch.randn(8192, cfg.K, device=dev).to(cfg.dtype)
